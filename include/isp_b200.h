@@ -1,0 +1,174 @@
+/*
+ * isp_b200.h — C ABI of the B200 (sm_100a) quantized-linear hot path.
+ *
+ * Plain C: raw device pointers, sizes, host scalars and a CUDA stream.  No
+ * function allocates, synchronizes or throws; every one validates shapes,
+ * dtypes and alignment on the host before launching and returns an
+ * isp_status.  Work is stream-ordered on the caller's stream, so calls can be
+ * captured into CUDA graphs.  All matrices are row-major and contiguous.
+ *
+ * Each entry point names the reference interface it replaces
+ * (xiro2416/inspark_proper_format, paths relative to its root).
+ */
+#ifndef ISP_B200_H
+#define ISP_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; 0 is the legacy default stream. */
+typedef struct CUstream_st *isp_stream_t;
+
+enum isp_status {
+  ISP_OK = 0,
+  ISP_ERR_SHAPE = 1,    /* a size is out of the supported range           */
+  ISP_ERR_ALIGN = 2,    /* a pointer/row stride breaks a 16-byte rule      */
+  ISP_ERR_DTYPE = 3,    /* unsupported dtype combination                   */
+  ISP_ERR_ARCH = 4,     /* current device is not sm_100                    */
+  ISP_ERR_LAUNCH = 5,   /* the CUDA launch itself failed                   */
+  ISP_ERR_TIMEOUT = 6,  /* a bounded device-side wait expired (see below)  */
+  ISP_ERR_ARG = 7       /* a required pointer is NULL / bad enum value     */
+};
+
+enum isp_dtype {
+  ISP_BF16 = 0, ISP_F32 = 1, ISP_F16 = 2, ISP_E4M3 = 3, ISP_I8 = 4, ISP_E2M1 = 5, ISP_I32 = 6
+};
+
+/* Row normalization applied before quantization. */
+enum isp_norm {
+  ISP_NORM_NONE = 0,
+  /* gpt_fast RMSNorm: bf16/f32(x*rsqrt(mean(x^2)+eps)) * gamma (FP32)
+     models/indextts2/upstream/s2mel/modules/gpt_fast/model.py:246-258 */
+  ISP_NORM_RMS_GPTFAST = 1,
+  /* Qwen-style RMSNorm: round_to_input_dtype(x*rsqrt(mean(x^2)+eps)*gamma)
+     models/indextts2/dspark/draft.py:12-23 */
+  ISP_NORM_RMS_QWEN = 2,
+  /* Zipformer BiasNorm: round_to_input_dtype(x * mean((x-b)^2)^-1/2 * out_mul)
+     models/zipvoice/reference/models/modules/scaling.py:337-370 */
+  ISP_NORM_BIAS = 3
+};
+
+/* Activation quantization formats. */
+enum isp_qfmt {
+  /* codes = e4m3_rne(clamp(y / scale, +-448)); build/unified_acoustic_export.py:22-36 */
+  ISP_Q_E4M3_STATIC = 0,
+  /* s[m] = max(amax_m/448, 1e-12); codes = e4m3(y / s[m]); ops/triton/fp8.py:11-17 */
+  ISP_Q_E4M3_ROW = 1,
+  /* codes = clamp(rne(y / smooth[k] / scale), -128, 127);
+     build/unified_acoustic_export.py:160-162, 27-29 */
+  ISP_Q_INT8_STATIC = 2,
+  /* NVFP4: 16-element blocks, E4M3 block scale e4m3(amax_b / (6 g)), E2M1
+     codes of y / (s_b g) packed low nibble = even k;
+     scripts/export_nvfp4_weights.py:25-42 */
+  ISP_Q_NVFP4 = 3
+};
+
+int isp_version(void);
+const char *isp_status_string(int status);
+
+/* Returns ISP_OK when the current CUDA device is a compute capability 10.0
+   part the library was built for, ISP_ERR_ARCH otherwise. */
+int isp_device_check(void);
+
+/* Device-side error word shared by all kernels with bounded waits.  A wait
+   that gives up records ISP_ERR_TIMEOUT there and the kernel returns early.
+   Reads (and with clear != 0, resets) the word for the current device;
+   synchronizes `stream`. */
+int isp_read_device_error(int *error_out, int clear, isp_stream_t stream);
+
+/*
+ * Fused row normalization -> quantization.
+ *
+ * Replaces: RMSNorm/BiasNorm followed by the separate quantize step of
+ *   _QDQ.forward            build/unified_acoustic_export.py:22-36
+ *   inspark_custom::fp8_quantize  ops/tensorrt/cfm_gated_up_plugin.py:17-31
+ *   _quantize (per-row)     ops/triton/fp8.py:11-17
+ *   ExportWeightOp INT8 SmoothQuant input path  build/unified_acoustic_export.py:160-162
+ *   NVFP4 dynamic activation quantization  quantization/nvfp4.py:66
+ *
+ * x:      [M, K] in x_dtype (ISP_BF16 or ISP_F32); K % 16 == 0.
+ * gamma:  [K] FP32 (RMS kinds), bias: [K] FP32 (ISP_NORM_BIAS), else NULL.
+ * out_mul: exp(log_scale) for ISP_NORM_BIAS (ignored otherwise).
+ * scale:  ISP_Q_E4M3_STATIC / ISP_Q_INT8_STATIC: the per-tensor scale;
+ *         ISP_Q_NVFP4: the FP32 global scale g; ignored for ISP_Q_E4M3_ROW.
+ * smooth: [K] FP32 SmoothQuant divisor (ISP_Q_INT8_STATIC) or NULL.
+ * codes:  [M, K] uint8/int8 codes, or [M, K/2] packed E2M1 for NVFP4.
+ * scales_out: FP32 [M] (ISP_Q_E4M3_ROW), E4M3 [M, K/16] (ISP_Q_NVFP4), else NULL.
+ */
+int isp_norm_quant(const void *x, int x_dtype, int64_t M, int K,
+                   const float *gamma, const float *bias, float eps, float out_mul,
+                   int norm_kind, int qfmt, float scale, const float *smooth,
+                   void *codes, void *scales_out, isp_stream_t stream);
+
+/*
+ * BigVGAN anti-aliased Snake activation: 2x 12-tap polyphase upsample with
+ * replicate padding, Snake v + inv_beta[c] * sin(alpha[c] v)^2, 12-tap
+ * stride-2 replicate-padded low-pass, fused in one pass over x.
+ *
+ * Replaces: Activation1d  models/indextts2/upstream/s2mel/modules/bigvgan/alias_free_activation/torch/act.py:16-21
+ *   FusedAliasFree         ops/triton/alias_free.py:28-43 (_up_snake + _down)
+ *   inspark_custom::small_fir_activation[_tiled]  ops/tensorrt/vocoder_tiled_fir_plugin.py:11-36
+ *   inspark_custom::small_fir_activation_quantized  deployment/multibatch/fir_quant_plugin.py:11-26
+ *
+ * x: [rows, T] FP32 with rows = B*C and channel = row % C.
+ * up, down: 12 FP32 taps each.  alpha, inv_beta: [C] FP32 (linear alpha;
+ * inv_beta = 1/(beta + 1e-9)).
+ * out_dtype ISP_F32: y [rows, T] FP32.
+ * out_dtype ISP_I8: y = clamp(rint((v / smooth[c]) / scale), -128, 127) int8.
+ */
+int isp_fir_snake(const float *x, int64_t rows, int C, int64_t T,
+                  const float *up, const float *down, const float *alpha, const float *inv_beta,
+                  void *y, int out_dtype, const float *smooth, float scale, isp_stream_t stream);
+
+/*
+ * W8A8 scaled GEMM on tcgen05 tensor cores: out = epilogue(A[M,K] . W[N,K]^T).
+ *
+ * Replaces: _gemm/_reduce   ops/triton/fp8.py:19-45 (and ops.matrix.linear)
+ *   FP8Linear.forward       runtime/zipvoice_fp8/quantization.py:75-82
+ *   FusedProjectionResidual ops/tensorrt/zipvoice_fp8_b128/b128/residual_kernel.py:4-11
+ *   i8_residual             ops/tensorrt/zipvoice/a1007/b1/i8_residual_runtime_kernel.py:5-21
+ *   TRT native FP8 / INT8 GEMMs under explicit Q/DQ
+ *
+ * ab_dtype: ISP_E4M3 (FP32 accumulate) or ISP_I8 (exact int32 accumulate).
+ * K % 16 == 0, N % 16 == 0, A/W 16-byte aligned.
+ * v = ((acc * a_s[m]) * w_scale[n]) + bias[n] + residual[m, n], where a_s is
+ *   a_scale_rows[m] when given, else the scalar a_scale; w_scale NULL means 1.
+ * out: out_dtype ISP_BF16 / ISP_F16 / ISP_F32 value, or ISP_E4M3 codes of
+ *   clamp(v * out_inv_scale, +-448) (next-layer static requant by the
+ *   reciprocal scale, as the residual plugin's `Inv`).
+ * out2 (optional): E4M3 codes of clamp(v * out2_inv_scale, +-448) — the
+ *   second output of the residual plugin.  residual: [M, N] in residual_dtype
+ *   (ISP_F32 or ISP_BF16) or NULL.
+ */
+int isp_scaled_gemm(const void *A, const void *W, int ab_dtype, int64_t M, int N, int K,
+                    float a_scale, const float *a_scale_rows, const float *w_scale,
+                    const float *bias, const void *residual, int residual_dtype,
+                    void *out, int out_dtype, float out_inv_scale, void *out2, float out2_inv_scale,
+                    isp_stream_t stream);
+
+/*
+ * CFM gated-up: h = silu(A.W1^T * s1[n]) * (A.W3^T * s3[n]), then static E4M3
+ * requant q = e4m3(clamp(h * (1/out_scale), +-448)).
+ *
+ * Replaces: _paired / GatedUp  ops/triton/cfm_gated_up.py:7-51
+ *   inspark_custom::fp8_gated_up  ops/tensorrt/cfm_gated_up_plugin.py:33-49
+ *   _interleaved / fp8_gated_up_interleaved  ops/triton/cfm_interleaved.py:19-55,
+ *                                            ops/tensorrt/cfm_interleaved_plugin.py:15-41
+ *
+ * interleaved == 0: W1, W3 are [N, K] E4M3 and s1, s3 [N] FP32.
+ * interleaved != 0: W1 is [2N, K] with row 2n = gate n, row 2n+1 = up n;
+ *   s1 is [2N]; W3 and s3 must be NULL.
+ * out_dtype ISP_E4M3: codes [M, N]; ISP_F32: q * out_scale (DEQUANT=True).
+ */
+int isp_gated_up(const void *A, const void *W1, const void *W3, int interleaved,
+                 int64_t M, int N, int K, const float *s1, const float *s3,
+                 float out_scale, void *out, int out_dtype, isp_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ISP_B200_H */

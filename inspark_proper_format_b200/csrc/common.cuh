@@ -1,0 +1,108 @@
+// Shared device/host helpers for the sm_100a kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/isp_b200.h"
+
+#define ISP_HD __host__ __device__ __forceinline__
+#define ISP_D __device__ __forceinline__
+
+namespace isp {
+
+// ---------------------------------------------------------------------------
+// Host-side validation helpers
+// ---------------------------------------------------------------------------
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Checks (once per device) that the current device is compute capability 10.x.
+int check_device();
+
+// Maps the last CUDA launch error to a status code (clears sticky launch error).
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ISP_OK : ISP_ERR_LAUNCH;
+}
+
+// Device error word (one per device; the library is a single translation unit).
+__device__ int g_device_error = 0;
+
+// ---------------------------------------------------------------------------
+// Number formats (device).  E4M3 conversion uses the hardware cvt with
+// round-to-nearest-even; callers clamp to +-448 first, as the reference does.
+// ---------------------------------------------------------------------------
+// Packs two floats into two E4M3 bytes: `lo` goes to bits 0-7, `hi` to 8-15.
+ISP_D uint16_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+ISP_D float e4m3_to_f32(uint8_t code) {
+  uint16_t packed = code;
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(packed));
+  __half h = __ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu));
+  return __half2float(h);
+}
+
+ISP_D float clamp448(float v) { return fminf(fmaxf(v, -448.f), 448.f); }
+
+// E2M1 code (sign in bit 3) of v: midpoints go to the even code, magnitudes
+// above 6 saturate, the sign bit is (v < 0).  Written from the format
+// definition; decision points 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.
+ISP_D uint32_t e2m1_code(float v) {
+  float a = fabsf(v);
+  uint32_t m = (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) +
+               (a >= 3.5f) + (a > 5.0f);
+  return m | (v < 0.f ? 8u : 0u);
+}
+
+ISP_D int8_t int8_rne_sat(float v) {
+  int q = __float2int_rn(v);
+  q = q < -128 ? -128 : (q > 127 ? 127 : q);
+  return static_cast<int8_t>(q);
+}
+
+ISP_D float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// ---------------------------------------------------------------------------
+// Global-memory vector helpers
+// ---------------------------------------------------------------------------
+ISP_D uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+ISP_D void bf16x8_to_f32(const uint4& v, float* out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(w[i] << 16);
+    out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Bounded waits: every spin gives up after ~1 s of %globaltimer, records
+// ISP_ERR_TIMEOUT in g_device_error and reports failure to the caller, which
+// then unwinds without touching the data path.
+// ---------------------------------------------------------------------------
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+ISP_D uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+ISP_D void record_timeout() { atomicExch(&g_device_error, (int)ISP_ERR_TIMEOUT); }
+
+}  // namespace isp

@@ -1,0 +1,534 @@
+// W8A8 (E4M3 / INT8) GEMM on 5th-generation tensor cores (tcgen05), sm_100a.
+//
+// out[M, N] = epilogue(A[M, K] . B[N, K]^T), both operands K-major 8-bit.
+//
+// Persistent, warp-specialized CTA (192 threads, one CTA per SM):
+//   warp 0      TMA producer: A and B tiles (BK = 128 bytes of K, 128-byte
+//               swizzle) into a kStages-deep shared-memory ring.
+//   warp 1      TMEM allocator + MMA issuer: one elected thread issues
+//               tcgen05.mma (M = 128, N = BN, K = 32 per instruction) into one
+//               of two TMEM accumulators, so the epilogue of tile i overlaps
+//               the main loop of tile i+1.
+//   warps 2..5  epilogue: tcgen05.ld (32 lanes x 32 columns per load), fused
+//               scale / bias / residual / SwiGLU / requant, 128-byte swizzled
+//               staging and TMA stores.
+// Every mbarrier wait is bounded (~1 s); on expiry the waiting thread records
+// ISP_ERR_TIMEOUT in g_device_error, raises the CTA abort flag, and all roles
+// unwind to the common exit, which drains in-flight TMA/MMA work and frees TMEM.
+#pragma once
+
+#include "common.cuh"
+
+namespace isp {
+namespace gemm {
+
+constexpr int kBM = 128;
+constexpr int kBK = 128;          // bytes (= elements) of K per stage
+constexpr int kThreads = 192;
+constexpr int kEpiWarp0 = 2;
+
+enum EpiKind { EPI_SCALE = 0, EPI_SWIGLU_PAIRED = 1, EPI_SWIGLU_INTERLEAVED = 2 };
+enum OutKind { OUT_BF16 = 0, OUT_F16 = 1, OUT_F32 = 2, OUT_E4M3 = 3 };
+
+ISP_HD int out_bytes(int out) { return out == OUT_F32 ? 4 : (out == OUT_E4M3 ? 1 : 2); }
+
+struct Params {
+  int M, N, K;            // N = logical output columns
+  int m_tiles, n_tiles, k_blocks;
+  float a_scale;
+  const float* a_scale_rows;
+  const float* w_scale;   // [N] scale (EPI_SCALE), s1 [N] or interleaved S [2N]
+  const float* w_scale2;  // s3 [N] (paired SwiGLU)
+  const float* bias;
+  const void* residual;
+  int residual_f32;
+  float out_inv;          // E4M3 output multiplier
+  float out_scale;        // SwiGLU dequant multiplier (F32 output)
+  void* out2;             // residual-dual E4M3 output
+  float out2_inv;
+};
+
+template <int kBN, int kStages>
+struct Smem {
+  static constexpr int kABytes = kBM * kBK;
+  static constexpr int kBBytes = kBN * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStagingBytes = 4 * 2 * 32 * 128;  // 4 warps x 2 buffers x (32 rows x 128 B)
+  static constexpr int kBarOffset = kStages * kStageBytes + kStagingBytes;
+  static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers/flags + alignment slack
+};
+
+// ----------------------------------------------------------------------------
+// PTX wrappers
+// ----------------------------------------------------------------------------
+ISP_D uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+ISP_D void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+ISP_D void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+ISP_D void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+ISP_D bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: true on success; false after the time limit or when another
+// role of this CTA has already given up (abort flag).
+ISP_D bool wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - start > kWaitLimitNs) {
+        record_timeout();
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+ISP_D void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+ISP_D void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+ISP_D void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+ISP_D void bulk_wait_read_le1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+ISP_D void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+ISP_D void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+ISP_D void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+ISP_D void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+ISP_D void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand tile, 128-byte rows, 128-byte swizzle, 8-row groups 1024 B apart.
+ISP_D uint64_t smem_desc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);   // start address
+  d |= static_cast<uint64_t>(1) << 16;                  // leading byte offset (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;          // stride byte offset: 8 rows x 128 B
+  d |= static_cast<uint64_t>(1) << 46;                  // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;                  // 128-byte swizzle
+  return d;
+}
+
+template <bool kInt8, int kBN>
+ISP_HD uint32_t instr_desc() {
+  // D format (F32 = 1, S32 = 2), A/B format (E4M3 = 0, signed int8 = 1), K-major A and B,
+  // N >> 3 at bit 17, M >> 4 at bit 24.
+  return (kInt8 ? (2u << 4) : (1u << 4)) | (kInt8 ? (1u << 7) | (1u << 10) : 0u) |
+         (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+
+template <bool kInt8>
+ISP_D void mma_issue(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  if constexpr (kInt8) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  }
+}
+ISP_D void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 TMEM lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
+ISP_D void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+ISP_D void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ----------------------------------------------------------------------------
+// Epilogue helpers
+// ----------------------------------------------------------------------------
+template <bool kInt8>
+ISP_D float acc_value(uint32_t bits) {
+  if constexpr (kInt8) return static_cast<float>(static_cast<int32_t>(bits));
+  else return __uint_as_float(bits);
+}
+
+ISP_D uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+ISP_D uint32_t pack_f16(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+ISP_D uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+  return static_cast<uint32_t>(e4m3x2(clamp448(a), clamp448(b))) |
+         (static_cast<uint32_t>(e4m3x2(clamp448(c), clamp448(d))) << 16);
+}
+
+// Write one thread's 128-byte row of the 32 x 128 B staging box (128-byte swizzle).
+ISP_D void stage_row(uint8_t* stage, int row, const uint32_t (&w)[32]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4 v = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    *reinterpret_cast<uint4*>(stage + row * 128 + ((j ^ (row & 7)) << 4)) = v;
+  }
+}
+
+ISP_D void load_f32x32(const float* p, float (&v)[32]) {   // 16-byte aligned, uniform across the warp
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 t = __ldg(reinterpret_cast<const float4*>(p) + j);
+    v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+  }
+}
+
+ISP_D float silu_mul(float g, float u) {
+  const float sig = __fdividef(1.f, 1.f + __expf(-g));
+  return __fmul_rn(__fmul_rn(g, sig), u);
+}
+
+// ----------------------------------------------------------------------------
+// The kernel
+// ----------------------------------------------------------------------------
+template <int kBN, int kStages, bool kInt8, int kEpi, int kOut>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_out,
+                const Params p) {
+  using L = Smem<kBN, kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* staging = smem + kStages * L::kStageBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty_bar = full_bar + kStages;
+  uint64_t* tfull_bar = empty_bar + kStages;     // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;          // [2]
+  uint64_t* drain_bar = tempty_bar + 2;          // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr int kTmemCols = 2 * kBN;             // two accumulators (power of two, >= 32)
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);              // one arrive per epilogue warp
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&tm_a);
+    prefetch_tmap(&tm_b);
+    if constexpr (kEpi == EPI_SWIGLU_PAIRED) prefetch_tmap(&tm_b2);
+    prefetch_tmap(&tm_out);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = p.m_tiles * p.n_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_phase[kStages];
+      bool armed[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) armed[s] = false, armed_phase[s] = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / p.n_tiles) * kBM;
+        const int nt = tile % p.n_tiles;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          uint8_t* sa = smem + stage * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          mbar_expect_tx(&full_bar[stage], L::kStageBytes);
+          armed[stage] = true;
+          armed_phase[stage] = phase;
+          tma_load_2d(sa, &tm_a, &full_bar[stage], kb * kBK, m0);
+          if constexpr (kEpi == EPI_SWIGLU_PAIRED) {
+            tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * (kBN / 2));
+            tma_load_2d(sb + (kBN / 2) * kBK, &tm_b2, &full_bar[stage], kb * kBK, nt * (kBN / 2));
+          } else {
+            tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * kBN);
+          }
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain: every armed stage's last load has landed before the CTA exits.
+      for (int s = 0; s < kStages; ++s)
+        if (armed[s]) wait_bounded(&full_bar[s], armed_phase[s], abort_flag);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc<kInt8, kBN>();
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        if (!wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bounded(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk) {
+            mma_issue<kInt8>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
+                             (kb | kk) != 0);
+          }
+          issued = true;
+          mma_commit(&empty_bar[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit(&tfull_bar[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      // Drain: all issued MMAs have completed before TMEM is released.
+      if (issued) {
+        mma_commit(drain_bar);
+        wait_bounded(drain_bar, 0, abort_flag);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - kEpiWarp0;             // 0..3
+    const int quarter = warp & 3;                // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    uint8_t* stage_base = staging + ew * (2 * 32 * 128);
+    int sbuf = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    constexpr int kOutCols = (kEpi == EPI_SCALE) ? kBN : kBN / 2;
+    constexpr int kChunkCols = 128 / (kOut == OUT_F32 ? 4 : (kOut == OUT_E4M3 ? 1 : 2));
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
+      const int m0 = (tile / p.n_tiles) * kBM;
+      const int n0 = (tile % p.n_tiles) * kOutCols;
+      if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int m = m0 + row_in_tile;
+      const bool row_ok = m < p.M;
+      float sa = p.a_scale;
+      if (p.a_scale_rows != nullptr && row_ok) sa = __ldg(p.a_scale_rows + m);
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+
+#pragma unroll 1
+      for (int c0 = 0; c0 < kOutCols; c0 += kChunkCols) {
+        uint32_t w[32];
+#pragma unroll
+        for (int sub = 0; sub < kChunkCols / 32; ++sub) {
+          const int col = c0 + sub * 32;         // first output column of these 32, tile-relative
+          const int n = n0 + col;                // global output column
+          float v[32];
+          if constexpr (kEpi == EPI_SCALE) {
+            uint32_t r[32];
+            tmem_ld32(t_row + col, r);
+            tmem_ld_wait();
+            float ws[32], bs[32];
+            const bool cols_ok = n + 32 <= p.N;
+            if (p.w_scale != nullptr && cols_ok) load_f32x32(p.w_scale + n, ws);
+            if (p.bias != nullptr && cols_ok) load_f32x32(p.bias + n, bs);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              // FP8: (acc * sa) * ws[n] (ops/triton/fp8.py:32); INT8: acc * (AS * WS[n])
+              // (i8_residual_runtime_kernel.py:18-20).  The order decides the rounding.
+              float t;
+              if (p.w_scale != nullptr) {
+                const float wsj = cols_ok ? ws[j] : (n + j < p.N ? __ldg(p.w_scale + n + j) : 0.f);
+                t = kInt8 ? __fmul_rn(acc_value<kInt8>(r[j]), __fmul_rn(sa, wsj))
+                          : __fmul_rn(__fmul_rn(acc_value<kInt8>(r[j]), sa), wsj);
+              } else {
+                t = __fmul_rn(acc_value<kInt8>(r[j]), sa);
+              }
+              if (p.bias != nullptr) t = __fadd_rn(t, cols_ok ? bs[j] : (n + j < p.N ? __ldg(p.bias + n + j) : 0.f));
+              v[j] = t;
+            }
+            if (p.residual != nullptr && row_ok) {
+              if (p.residual_f32) {
+                const float* rr = static_cast<const float*>(p.residual) + static_cast<int64_t>(m) * p.N + n;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (n + j < p.N) v[j] = __fadd_rn(v[j], __ldg(rr + j));
+              } else {
+                const __nv_bfloat16* rr = static_cast<const __nv_bfloat16*>(p.residual) + static_cast<int64_t>(m) * p.N + n;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (n + j < p.N) v[j] = __fadd_rn(v[j], __bfloat162float(rr[j]));
+              }
+            }
+            if (p.out2 != nullptr && row_ok) {
+              uint8_t* o2 = static_cast<uint8_t*>(p.out2) + static_cast<int64_t>(m) * p.N + n;
+              uint32_t q[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                q[j] = pack_e4m3x4(__fmul_rn(v[4 * j], p.out2_inv), __fmul_rn(v[4 * j + 1], p.out2_inv),
+                                   __fmul_rn(v[4 * j + 2], p.out2_inv), __fmul_rn(v[4 * j + 3], p.out2_inv));
+              if (n + 32 <= p.N) {
+                reinterpret_cast<uint4*>(o2)[0] = make_uint4(q[0], q[1], q[2], q[3]);
+                reinterpret_cast<uint4*>(o2)[1] = make_uint4(q[4], q[5], q[6], q[7]);
+              } else {
+                for (int j = 0; j < 32 && n + j < p.N; ++j) o2[j] = static_cast<uint8_t>(q[j >> 2] >> (8 * (j & 3)));
+              }
+            }
+          } else {
+            // SwiGLU: gate/up accumulator columns for output columns col..col+31
+            uint32_t g[32], u[32];
+            float s_g[32], s_u[32];
+            if constexpr (kEpi == EPI_SWIGLU_PAIRED) {
+              tmem_ld32(t_row + col, g);
+              tmem_ld32(t_row + kBN / 2 + col, u);
+              tmem_ld_wait();
+              if (n < p.N) {                    // N % 32 == 0: a 32-column group is all in or all out
+                load_f32x32(p.w_scale + n, s_g);
+                load_f32x32(p.w_scale2 + n, s_u);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) s_g[j] = s_u[j] = 0.f;
+              }
+            } else {
+              uint32_t lo[32], hi[32];
+              tmem_ld32(t_row + 2 * col, lo);
+              tmem_ld32(t_row + 2 * col + 32, hi);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                g[j] = lo[2 * j]; u[j] = lo[2 * j + 1];
+                g[16 + j] = hi[2 * j]; u[16 + j] = hi[2 * j + 1];
+              }
+              float sl[32], sh[32];
+              if (n < p.N) {
+                load_f32x32(p.w_scale + 2 * n, sl);
+                load_f32x32(p.w_scale + 2 * n + 32, sh);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) sl[j] = sh[j] = 0.f;
+              }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                s_g[j] = sl[2 * j]; s_u[j] = sl[2 * j + 1];
+                s_g[16 + j] = sh[2 * j]; s_u[16 + j] = sh[2 * j + 1];
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float gv = __fmul_rn(__uint_as_float(g[j]), s_g[j]);
+              const float uv = __fmul_rn(__uint_as_float(u[j]), s_u[j]);
+              v[j] = clamp448(__fmul_rn(silu_mul(gv, uv), p.out_inv));
+            }
+            if constexpr (kOut == OUT_F32) {
+              // DEQUANT: e4m3 round trip times the output scale
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) {
+                const uint16_t q2 = e4m3x2(v[j], v[j + 1]);
+                v[j] = __fmul_rn(e4m3_to_f32(static_cast<uint8_t>(q2 & 0xFF)), p.out_scale);
+                v[j + 1] = __fmul_rn(e4m3_to_f32(static_cast<uint8_t>(q2 >> 8)), p.out_scale);
+              }
+            }
+          }
+          // ---- convert this sub-block into its words of the 128-byte row
+          if constexpr (kOut == OUT_F32) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
+          } else if constexpr (kOut == OUT_BF16) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w[sub * 16 + j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+          } else if constexpr (kOut == OUT_F16) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w[sub * 16 + j] = pack_f16(v[2 * j], v[2 * j + 1]);
+          } else {  // OUT_E4M3
+            if constexpr (kEpi == EPI_SCALE) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(v[j], p.out_inv);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) w[sub * 8 + j] = pack_e4m3x4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          }
+        }
+        // ---- stage + TMA store of the 32-row x 128-byte box
+        uint8_t* st = stage_base + sbuf * (32 * 128);
+        if (lane == 0) bulk_wait_read_le1();     // the store that last used this buffer has read it
+        __syncwarp();
+        stage_row(st, lane, w);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && m0 + quarter * 32 < p.M) {   // boxes wholly below row M are skipped
+          tma_store_2d(&tm_out, st, n0 + c0, m0 + quarter * 32);
+          bulk_commit();
+        }
+        sbuf ^= 1;
+      }
+      // accumulator fully read: hand it back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
+  }
+}
+
+}  // namespace gemm
+}  // namespace isp

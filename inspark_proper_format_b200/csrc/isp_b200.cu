@@ -1,0 +1,303 @@
+// C-ABI entry points of libisp_b200.so (single translation unit: every kernel
+// header is included here so the device error word is shared).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "fir.cuh"
+#include "gemm_sm100.cuh"
+#include "norm_quant.cuh"
+
+namespace isp {
+
+int check_device() {
+  static std::mutex mu;
+  static int cached[64];
+  static bool init = false;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ISP_ERR_ARCH;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!init) {
+    for (int& c : cached) c = -1;
+    init = true;
+  }
+  if (dev < 0 || dev >= 64) return ISP_ERR_ARCH;
+  if (cached[dev] < 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cached[dev] = (major == 10 && minor == 0) ? ISP_OK : ISP_ERR_ARCH;
+  }
+  return cached[dev];
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+namespace gemm {
+
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor [outer, inner] with a (box_inner x box_outer) box and 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+              uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+  EncodeFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * static_cast<uint64_t>(elem_bytes)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_out_map(CUtensorMap* map, void* out, int out_kind, int64_t M, int N) {
+  const int eb = out_bytes(out_kind);
+  const CUtensorMapDataType dt = out_kind == OUT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : out_kind == OUT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : out_kind == OUT_F16  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  return make_map(map, out, dt, eb, static_cast<uint64_t>(N), static_cast<uint64_t>(M),
+                  static_cast<uint32_t>(128 / eb), 32);
+}
+
+template <int kBN, int kStages, bool kInt8, int kEpi, int kOut>
+int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, const CUtensorMap& o,
+           const Params& p, cudaStream_t stream) {
+  auto kern = gemm_kernel<kBN, kStages, kInt8, kEpi, kOut>;
+  constexpr int kSmem = Smem<kBN, kStages>::kBytes;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+      return ISP_ERR_LAUNCH;
+    configured[dev] = true;
+  }
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, kThreads, kSmem, stream>>>(a, b, b2, o, p);
+  return launch_status();
+}
+
+constexpr int kBN = 256;
+constexpr int kStages = 4;
+
+template <bool kInt8>
+int dispatch_scale_out(int out_kind, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
+                       const Params& p, cudaStream_t s) {
+  switch (out_kind) {
+    case OUT_BF16: return launch<kBN, kStages, kInt8, EPI_SCALE, OUT_BF16>(a, b, b, o, p, s);
+    case OUT_F16: return launch<kBN, kStages, kInt8, EPI_SCALE, OUT_F16>(a, b, b, o, p, s);
+    case OUT_F32: return launch<kBN, kStages, kInt8, EPI_SCALE, OUT_F32>(a, b, b, o, p, s);
+    case OUT_E4M3: return launch<kBN, kStages, kInt8, EPI_SCALE, OUT_E4M3>(a, b, b, o, p, s);
+    default: return ISP_ERR_DTYPE;
+  }
+}
+
+int out_kind_of(int dtype) {
+  switch (dtype) {
+    case ISP_BF16: return OUT_BF16;
+    case ISP_F16: return OUT_F16;
+    case ISP_F32: return OUT_F32;
+    case ISP_E4M3: return OUT_E4M3;
+    default: return -1;
+  }
+}
+
+}  // namespace gemm
+}  // namespace isp
+
+extern "C" {
+
+int isp_version(void) { return 100; }
+
+const char* isp_status_string(int status) {
+  switch (status) {
+    case ISP_OK: return "ok";
+    case ISP_ERR_SHAPE: return "unsupported shape";
+    case ISP_ERR_ALIGN: return "pointer or row stride not 16-byte aligned";
+    case ISP_ERR_DTYPE: return "unsupported dtype";
+    case ISP_ERR_ARCH: return "current device is not an sm_100 (B200) GPU";
+    case ISP_ERR_LAUNCH: return "CUDA launch failed";
+    case ISP_ERR_TIMEOUT: return "a bounded device-side wait expired";
+    case ISP_ERR_ARG: return "invalid argument";
+    default: return "unknown status";
+  }
+}
+
+int isp_device_check(void) { return isp::check_device(); }
+
+int isp_read_device_error(int* error_out, int clear, isp_stream_t stream) {
+  if (error_out == nullptr) return ISP_ERR_ARG;
+  if (int st = isp::check_device()) return st;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return ISP_ERR_LAUNCH;
+  int value = 0;
+  if (cudaMemcpyFromSymbol(&value, isp::g_device_error, sizeof(int)) != cudaSuccess) return ISP_ERR_LAUNCH;
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(isp::g_device_error, &zero, sizeof(int)) != cudaSuccess) return ISP_ERR_LAUNCH;
+  }
+  *error_out = value;
+  return ISP_OK;
+}
+
+int isp_norm_quant(const void* x, int x_dtype, int64_t M, int K, const float* gamma,
+                   const float* bias, float eps, float out_mul, int norm_kind, int qfmt,
+                   float scale, const float* smooth, void* codes, void* scales_out,
+                   isp_stream_t stream) {
+  if (x == nullptr || codes == nullptr) return ISP_ERR_ARG;
+  if (x_dtype != ISP_BF16 && x_dtype != ISP_F32) return ISP_ERR_DTYPE;
+  if (M < 0 || K <= 0 || K % 16 != 0) return ISP_ERR_SHAPE;
+  if (norm_kind < ISP_NORM_NONE || norm_kind > ISP_NORM_BIAS) return ISP_ERR_ARG;
+  if (qfmt < ISP_Q_E4M3_STATIC || qfmt > ISP_Q_NVFP4) return ISP_ERR_ARG;
+  if ((norm_kind == ISP_NORM_RMS_GPTFAST || norm_kind == ISP_NORM_RMS_QWEN) && gamma == nullptr)
+    return ISP_ERR_ARG;
+  if (norm_kind == ISP_NORM_BIAS && bias == nullptr) return ISP_ERR_ARG;
+  if ((qfmt == ISP_Q_E4M3_ROW || qfmt == ISP_Q_NVFP4) && scales_out == nullptr) return ISP_ERR_ARG;
+  if (qfmt != ISP_Q_E4M3_ROW && !(scale > 0.f)) return ISP_ERR_ARG;
+  if (!isp::aligned16(x) || !isp::aligned16(codes)) return ISP_ERR_ALIGN;
+  if ((gamma && !isp::aligned16(gamma)) || (bias && !isp::aligned16(bias)) ||
+      (smooth && !isp::aligned16(smooth)))
+    return ISP_ERR_ALIGN;
+  if (qfmt == ISP_Q_NVFP4 && (reinterpret_cast<uintptr_t>(scales_out) & 1)) return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  if (M == 0) return ISP_OK;
+  isp::NormQuantParams p{x, M, K, gamma, bias, eps, out_mul, scale, smooth, codes, scales_out};
+  return x_dtype == ISP_BF16 ? isp::launch_norm_quant_kind<true>(norm_kind, qfmt, p, stream)
+                             : isp::launch_norm_quant_kind<false>(norm_kind, qfmt, p, stream);
+}
+
+int isp_fir_snake(const float* x, int64_t rows, int C, int64_t T, const float* up,
+                  const float* down, const float* alpha, const float* inv_beta, void* y,
+                  int out_dtype, const float* smooth, float scale, isp_stream_t stream) {
+  if (!x || !up || !down || !alpha || !inv_beta || !y) return ISP_ERR_ARG;
+  if (out_dtype != ISP_F32 && out_dtype != ISP_I8) return ISP_ERR_DTYPE;
+  if (out_dtype == ISP_I8 && (smooth == nullptr || !(scale > 0.f))) return ISP_ERR_ARG;
+  if (rows < 0 || C <= 0 || T <= 0 || (rows % C) != 0) return ISP_ERR_SHAPE;
+  if (int st = isp::check_device()) return st;
+  if (rows == 0) return ISP_OK;
+  const int64_t tiles = (T + isp::kFirTile - 1) / isp::kFirTile;
+  const int64_t blocks = rows * tiles;
+  if (blocks > 0x7FFFFFFFll) return ISP_ERR_SHAPE;
+  isp::FirParams p{x, rows, C, T, tiles, up, down, alpha, inv_beta, y, smooth, scale};
+  if (out_dtype == ISP_F32)
+    isp::fir_snake_kernel<false><<<static_cast<unsigned>(blocks), isp::kFirThreads, 0, stream>>>(p);
+  else
+    isp::fir_snake_kernel<true><<<static_cast<unsigned>(blocks), isp::kFirThreads, 0, stream>>>(p);
+  return isp::launch_status();
+}
+
+int isp_scaled_gemm(const void* A, const void* W, int ab_dtype, int64_t M, int N, int K, float a_scale,
+                    const float* a_scale_rows, const float* w_scale, const float* bias, const void* residual,
+                    int residual_dtype, void* out, int out_dtype, float out_inv_scale, void* out2,
+                    float out2_inv_scale, isp_stream_t stream) {
+  using namespace isp::gemm;
+  if (A == nullptr || W == nullptr || out == nullptr) return ISP_ERR_ARG;
+  if (ab_dtype != ISP_E4M3 && ab_dtype != ISP_I8) return ISP_ERR_DTYPE;
+  const int out_kind = out_kind_of(out_dtype);
+  if (out_kind < 0) return ISP_ERR_DTYPE;
+  if (residual != nullptr && residual_dtype != ISP_F32 && residual_dtype != ISP_BF16) return ISP_ERR_DTYPE;
+  if (M < 0 || M > 0x7FFFFFFFll || N <= 0 || K <= 0 || K % 16 != 0 || N % 16 != 0) return ISP_ERR_SHAPE;
+  if (!isp::aligned16(A) || !isp::aligned16(W) || !isp::aligned16(out)) return ISP_ERR_ALIGN;
+  if ((w_scale && !isp::aligned16(w_scale)) || (bias && !isp::aligned16(bias)) || (out2 && !isp::aligned16(out2)))
+    return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  if (M == 0) return ISP_OK;
+  CUtensorMap ta, tb, to;
+  if (!make_map(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, kBK, kBM) ||
+      !make_map(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, kBK, kBN) || !make_out_map(&to, out, out_kind, M, N))
+    return ISP_ERR_ALIGN;
+  Params p{};
+  p.M = static_cast<int>(M);
+  p.N = N;
+  p.K = K;
+  p.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  p.n_tiles = (N + kBN - 1) / kBN;
+  p.k_blocks = (K + kBK - 1) / kBK;
+  p.a_scale = a_scale;
+  p.a_scale_rows = a_scale_rows;
+  p.w_scale = w_scale;
+  p.bias = bias;
+  p.residual = residual;
+  p.residual_f32 = residual_dtype == ISP_F32;
+  p.out_inv = out_inv_scale;
+  p.out2 = out2;
+  p.out2_inv = out2_inv_scale;
+  return ab_dtype == ISP_I8 ? dispatch_scale_out<true>(out_kind, ta, tb, to, p, stream)
+                            : dispatch_scale_out<false>(out_kind, ta, tb, to, p, stream);
+}
+
+int isp_gated_up(const void* A, const void* W1, const void* W3, int interleaved, int64_t M, int N, int K,
+                 const float* s1, const float* s3, float out_scale, void* out, int out_dtype,
+                 isp_stream_t stream) {
+  using namespace isp::gemm;
+  if (A == nullptr || W1 == nullptr || s1 == nullptr || out == nullptr) return ISP_ERR_ARG;
+  if (interleaved ? (W3 != nullptr || s3 != nullptr) : (W3 == nullptr || s3 == nullptr)) return ISP_ERR_ARG;
+  if (out_dtype != ISP_E4M3 && out_dtype != ISP_F32) return ISP_ERR_DTYPE;
+  if (!(out_scale > 0.f)) return ISP_ERR_ARG;
+  if (M < 0 || M > 0x7FFFFFFFll || N <= 0 || K <= 0 || K % 16 != 0 || N % 32 != 0) return ISP_ERR_SHAPE;
+  if (!isp::aligned16(A) || !isp::aligned16(W1) || !isp::aligned16(out) || !isp::aligned16(s1) ||
+      (W3 && !isp::aligned16(W3)) || (s3 && !isp::aligned16(s3)))
+    return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  if (M == 0) return ISP_OK;
+  const int out_kind = out_dtype == ISP_E4M3 ? OUT_E4M3 : OUT_F32;
+  CUtensorMap ta, tb, tb2, to;
+  if (!make_map(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, kBK, kBM) || !make_out_map(&to, out, out_kind, M, N))
+    return ISP_ERR_ALIGN;
+  if (interleaved) {
+    if (!make_map(&tb, W1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, 2ull * N, kBK, kBN)) return ISP_ERR_ALIGN;
+    tb2 = tb;
+  } else {
+    if (!make_map(&tb, W1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, kBK, kBN / 2) ||
+        !make_map(&tb2, W3, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, kBK, kBN / 2))
+      return ISP_ERR_ALIGN;
+  }
+  Params p{};
+  p.M = static_cast<int>(M);
+  p.N = N;
+  p.K = K;
+  p.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  p.n_tiles = (N + kBN / 2 - 1) / (kBN / 2);
+  p.k_blocks = (K + kBK - 1) / kBK;
+  p.a_scale = 1.f;
+  p.w_scale = s1;
+  p.w_scale2 = s3;
+  p.out_inv = static_cast<float>(1.0 / static_cast<double>(out_scale));
+  p.out_scale = out_scale;
+  if (interleaved) {
+    return out_kind == OUT_E4M3
+               ? launch<kBN, kStages, false, EPI_SWIGLU_INTERLEAVED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
+               : launch<kBN, kStages, false, EPI_SWIGLU_INTERLEAVED, OUT_F32>(ta, tb, tb2, to, p, stream);
+  }
+  return out_kind == OUT_E4M3 ? launch<kBN, kStages, false, EPI_SWIGLU_PAIRED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
+                              : launch<kBN, kStages, false, EPI_SWIGLU_PAIRED, OUT_F32>(ta, tb, tb2, to, p, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,247 @@
+// Fused row normalization -> quantization (memory-bound, one warp per row).
+//
+// Each lane owns groups of 8 consecutive elements (group g = lane + 32 i), so
+// a warp streams 256 contiguous elements per step with 16-byte loads (BF16) or
+// two 16-byte loads (FP32).  The row statistic is accumulated in double from
+// FP32 squares and rounded once; every following step is one IEEE FP32
+// operation in the order of the reference module (see isp_b200.h for the
+// reference file:line of each mode).
+#pragma once
+
+#include "common.cuh"
+
+namespace isp {
+
+struct NormQuantParams {
+  const void* x;
+  int64_t M;
+  int K;
+  const float* gamma;
+  const float* bias;
+  float eps;
+  float out_mul;
+  float scale;          // static scale (E4M3 / INT8) or NVFP4 global scale
+  const float* smooth;  // INT8 SmoothQuant divisor or nullptr
+  void* codes;
+  void* scales_out;
+};
+
+ISP_D void load_param8(const float* base, int g, float (&w)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(base + g * 8));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(base + g * 8 + 4));
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+
+template <bool kBF16>
+ISP_D void load_group(const void* row, int g, float (&v)[8]) {
+  if constexpr (kBF16) {
+    uint4 raw = ldg_nc_v4(static_cast<const uint16_t*>(row) + g * 8);
+    bf16x8_to_f32(raw, v);
+  } else {
+    const float* p = static_cast<const float*>(row) + g * 8;
+    uint4 a = ldg_nc_v4(p), b = ldg_nc_v4(p + 4);
+    v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y);
+    v[2] = __uint_as_float(a.z); v[3] = __uint_as_float(a.w);
+    v[4] = __uint_as_float(b.x); v[5] = __uint_as_float(b.y);
+    v[6] = __uint_as_float(b.z); v[7] = __uint_as_float(b.w);
+  }
+}
+
+ISP_D double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+ISP_D float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// kGroups: max 8-element groups per lane kept in registers (K <= 256 * kGroups).
+template <bool kBF16, int kNorm, int kFmt, int kGroups>
+__global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= p.M) return;
+  const int K = p.K;
+  const int ngroups = K >> 3;
+  const void* xrow = kBF16 ? static_cast<const void*>(static_cast<const uint16_t*>(p.x) + row * K)
+                           : static_cast<const void*>(static_cast<const float*>(p.x) + row * K);
+
+  float v[kGroups][8];
+#pragma unroll
+  for (int i = 0; i < kGroups; ++i) {
+    const int g = lane + 32 * i;
+    if (g < ngroups) load_group<kBF16>(xrow, g, v[i]);
+  }
+
+  // ---- normalization ------------------------------------------------------
+  if constexpr (kNorm != ISP_NORM_NONE) {
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) {
+      const int g = lane + 32 * i;
+      if (g < ngroups) {
+        float b8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if constexpr (kNorm == ISP_NORM_BIAS) load_param8(p.bias, g, b8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float d = v[i][j];
+          if constexpr (kNorm == ISP_NORM_BIAS) d = __fsub_rn(d, b8[j]);
+          ss += static_cast<double>(__fmul_rn(d, d));
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    const float mean = __fdiv_rn(static_cast<float>(ss), static_cast<float>(K));
+    float r;
+    if constexpr (kNorm == ISP_NORM_BIAS) {
+      r = __fmul_rn(__fdiv_rn(1.f, __fsqrt_rn(mean)), p.out_mul);
+    } else {
+      r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+    }
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) {
+      const int g = lane + 32 * i;
+      if (g < ngroups) {
+        float gm[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+        if constexpr (kNorm == ISP_NORM_RMS_GPTFAST || kNorm == ISP_NORM_RMS_QWEN) load_param8(p.gamma, g, gm);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float y = __fmul_rn(v[i][j], r);
+          if constexpr (kNorm == ISP_NORM_RMS_GPTFAST) {
+            if constexpr (kBF16) y = bf16_round(y);
+            y = __fmul_rn(y, gm[j]);
+          } else if constexpr (kNorm == ISP_NORM_RMS_QWEN) {
+            y = __fmul_rn(y, gm[j]);
+            if constexpr (kBF16) y = bf16_round(y);
+          } else {
+            if constexpr (kBF16) y = bf16_round(y);
+          }
+          v[i][j] = y;
+        }
+      }
+    }
+  }
+
+  // ---- quantization -------------------------------------------------------
+  if constexpr (kFmt == ISP_Q_E4M3_STATIC || kFmt == ISP_Q_E4M3_ROW) {
+    float s = p.scale;
+    if constexpr (kFmt == ISP_Q_E4M3_ROW) {
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < kGroups; ++i)
+        if (lane + 32 * i < ngroups)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+      amax = warp_max(amax);
+      s = fmaxf(__fdiv_rn(amax, 448.f), 1e-12f);
+      if (lane == 0) static_cast<float*>(p.scales_out)[row] = s;
+    }
+    uint8_t* out = static_cast<uint8_t*>(p.codes) + row * K;
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) {
+      const int g = lane + 32 * i;
+      if (g < ngroups) {
+        uint32_t w[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float* q = &v[i][4 * h];
+          uint32_t lo = e4m3x2(clamp448(__fdiv_rn(q[0], s)), clamp448(__fdiv_rn(q[1], s)));
+          uint32_t hi = e4m3x2(clamp448(__fdiv_rn(q[2], s)), clamp448(__fdiv_rn(q[3], s)));
+          w[h] = lo | (hi << 16);
+        }
+        *reinterpret_cast<uint2*>(out + g * 8) = make_uint2(w[0], w[1]);
+      }
+    }
+  } else if constexpr (kFmt == ISP_Q_INT8_STATIC) {
+    int8_t* out = static_cast<int8_t*>(p.codes) + row * K;
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) {
+      const int g = lane + 32 * i;
+      if (g < ngroups) {
+        uint32_t w[2] = {0u, 0u};
+        float sm[8];
+        if (p.smooth != nullptr) load_param8(p.smooth, g, sm);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float y = v[i][j];
+          if (p.smooth != nullptr) y = __fdiv_rn(y, sm[j]);
+          const int8_t q = int8_rne_sat(__fdiv_rn(y, p.scale));
+          w[j >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(q)) << (8 * (j & 3));
+        }
+        *reinterpret_cast<uint2*>(out + g * 8) = make_uint2(w[0], w[1]);
+      }
+    }
+  } else {  // ISP_Q_NVFP4: lanes (2p, 2p+1) hold the two halves of one 16-element block
+    uint8_t* out = static_cast<uint8_t*>(p.codes) + row * (K / 2);
+    uint8_t* sf = static_cast<uint8_t*>(p.scales_out) + row * (K / 16);
+    const float gscale = p.scale;
+    const float six_g = __fmul_rn(6.f, gscale);
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) {
+      const int g = lane + 32 * i;
+      // Every lane runs the shuffle; lanes without a group contribute 0.
+      float amax = 0.f;
+      if (g < ngroups)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      if (g < ngroups) {
+        float sb = __fdiv_rn(amax, six_g);
+        if (sb == 0.f) sb = 1.f;
+        const uint16_t sc2 = e4m3x2(fminf(sb, 448.f), 0.f);
+        const uint8_t sc = static_cast<uint8_t>(sc2 & 0xFF);
+        const float denom = __fmul_rn(e4m3_to_f32(sc), gscale);
+        uint32_t packed = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) packed |= e2m1_code(__fdiv_rn(v[i][j], denom)) << (4 * j);
+        *reinterpret_cast<uint32_t*>(out + g * 4) = packed;
+        if ((g & 1) == 0) sf[g >> 1] = sc;
+      }
+    }
+  }
+}
+
+template <bool kBF16, int kNorm, int kFmt>
+int launch_norm_quant_groups(const NormQuantParams& p, cudaStream_t stream) {
+  const int per_lane = (p.K / 8 + 31) / 32;
+  const dim3 grid(static_cast<unsigned>((p.M + 7) / 8)), block(256);
+  if (per_lane <= 2) norm_quant_kernel<kBF16, kNorm, kFmt, 2><<<grid, block, 0, stream>>>(p);
+  else if (per_lane <= 4) norm_quant_kernel<kBF16, kNorm, kFmt, 4><<<grid, block, 0, stream>>>(p);
+  else if (per_lane <= 8) norm_quant_kernel<kBF16, kNorm, kFmt, 8><<<grid, block, 0, stream>>>(p);
+  else if (per_lane <= 16) norm_quant_kernel<kBF16, kNorm, kFmt, 16><<<grid, block, 0, stream>>>(p);
+  else if constexpr (kNorm == ISP_NORM_NONE) {
+    if (per_lane <= 32) norm_quant_kernel<kBF16, kNorm, kFmt, 32><<<grid, block, 0, stream>>>(p);
+    else return ISP_ERR_SHAPE;
+  } else {
+    return ISP_ERR_SHAPE;
+  }
+  return launch_status();
+}
+
+template <bool kBF16, int kNorm>
+int launch_norm_quant_fmt(int fmt, const NormQuantParams& p, cudaStream_t s) {
+  switch (fmt) {
+    case ISP_Q_E4M3_STATIC: return launch_norm_quant_groups<kBF16, kNorm, ISP_Q_E4M3_STATIC>(p, s);
+    case ISP_Q_E4M3_ROW: return launch_norm_quant_groups<kBF16, kNorm, ISP_Q_E4M3_ROW>(p, s);
+    case ISP_Q_INT8_STATIC: return launch_norm_quant_groups<kBF16, kNorm, ISP_Q_INT8_STATIC>(p, s);
+    case ISP_Q_NVFP4: return launch_norm_quant_groups<kBF16, kNorm, ISP_Q_NVFP4>(p, s);
+    default: return ISP_ERR_ARG;
+  }
+}
+
+template <bool kBF16>
+int launch_norm_quant_kind(int kind, int fmt, const NormQuantParams& p, cudaStream_t s) {
+  switch (kind) {
+    case ISP_NORM_NONE: return launch_norm_quant_fmt<kBF16, ISP_NORM_NONE>(fmt, p, s);
+    case ISP_NORM_RMS_GPTFAST: return launch_norm_quant_fmt<kBF16, ISP_NORM_RMS_GPTFAST>(fmt, p, s);
+    case ISP_NORM_RMS_QWEN: return launch_norm_quant_fmt<kBF16, ISP_NORM_RMS_QWEN>(fmt, p, s);
+    case ISP_NORM_BIAS: return launch_norm_quant_fmt<kBF16, ISP_NORM_BIAS>(fmt, p, s);
+    default: return ISP_ERR_ARG;
+  }
+}
+
+}  // namespace isp

@@ -1,0 +1,93 @@
+"""Fused norm -> quantize op (torch-level wrapper over ``isp_norm_quant``).
+
+New op proposed by the survey of the reference: it fuses the reference's
+separate normalization (RMSNorm / Qwen RMSNorm / BiasNorm) and quantization
+steps (static E4M3 ``_QDQ``, per-row ``_quantize``, INT8 SmoothQuant, NVFP4
+dynamic block quantization) into one memory-bound pass.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+KINDS = {"none": _lib.NORM_NONE, "rms_gptfast": _lib.NORM_RMS_GPTFAST,
+         "rms_qwen": _lib.NORM_RMS_QWEN, "bias": _lib.NORM_BIAS}
+FORMATS = {"e4m3": _lib.Q_E4M3_STATIC, "e4m3_row": _lib.Q_E4M3_ROW,
+           "int8": _lib.Q_INT8_STATIC, "nvfp4": _lib.Q_NVFP4}
+
+
+def _param(t, k, name):
+    if t is None:
+        return None
+    if t.dtype != torch.float32 or not t.is_cuda or t.numel() != k or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous CUDA FP32 tensor of {k} elements")
+    return t
+
+
+def norm_quant(x: torch.Tensor, *, kind: str = "rms_gptfast", fmt: str = "e4m3",
+               gamma: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+               eps: float = 1e-6, log_scale: torch.Tensor | float | None = None,
+               scale: float | None = None, smooth: torch.Tensor | None = None,
+               global_scale: float | None = None, out: torch.Tensor | None = None,
+               scales_out: torch.Tensor | None = None):
+    """Normalize the rows of ``x`` ([..., K], BF16 or FP32) and quantize them.
+
+    Returns ``(codes, scales)``:
+      * ``e4m3``: float8_e4m3fn codes of ``clamp(y / scale)``, scales None;
+      * ``e4m3_row``: codes and FP32 per-row scales ``max(amax/448, 1e-12)``;
+      * ``int8``: int8 codes of ``clamp(rne(y / smooth / scale))``, scales None;
+      * ``nvfp4``: uint8 [..., K/2] packed E2M1 (low nibble = even k) and
+        float8_e4m3fn [..., K/16] block scales, with ``global_scale`` g.
+    """
+    if kind not in KINDS or fmt not in FORMATS:
+        raise ValueError(f"unknown norm kind {kind!r} or format {fmt!r}")
+    if x.dtype not in (torch.bfloat16, torch.float32) or not x.is_cuda:
+        raise ValueError("norm_quant expects a CUDA BF16 or FP32 tensor")
+    x = x.contiguous()
+    k = x.shape[-1]
+    m = x.numel() // k if k else 0
+    if k % 16:
+        raise ValueError("the quantized dimension must be a multiple of 16")
+    gamma = _param(gamma, k, "gamma")
+    bias = _param(bias, k, "bias")
+    smooth = _param(smooth, k, "smooth")
+    out_mul = 1.0
+    if kind == "bias":
+        ls = log_scale if isinstance(log_scale, torch.Tensor) else torch.tensor(float(log_scale or 0.0))
+        out_mul = float(ls.detach().float().exp())
+    lead = x.shape[:-1]
+    if fmt == "nvfp4":
+        if global_scale is None:
+            raise ValueError("nvfp4 needs the FP32 global scale")
+        s = float(global_scale)
+        codes = out if out is not None else torch.empty(*lead, k // 2, device=x.device, dtype=torch.uint8)
+        scales = scales_out if scales_out is not None else torch.empty(*lead, k // 16, device=x.device,
+                                                                      dtype=torch.float8_e4m3fn)
+    else:
+        if fmt in ("e4m3", "int8"):
+            if scale is None:
+                raise ValueError(f"{fmt} needs a calibrated static scale")
+            s = float(scale)
+        else:
+            s = 0.0
+        dtype = torch.int8 if fmt == "int8" else torch.float8_e4m3fn
+        codes = out if out is not None else torch.empty(*lead, k, device=x.device, dtype=dtype)
+        scales = None
+        if fmt == "e4m3_row":
+            scales = scales_out if scales_out is not None else torch.empty(*lead, device=x.device,
+                                                                          dtype=torch.float32)
+    status = _lib.load().isp_norm_quant(
+        x.data_ptr(), _lib.BF16 if x.dtype == torch.bfloat16 else _lib.F32, m, k,
+        _lib.ptr(gamma), _lib.ptr(bias), float(eps), out_mul, KINDS[kind], FORMATS[fmt], s,
+        _lib.ptr(smooth), codes.data_ptr(), _lib.ptr(scales), _lib.stream_handle(x.device))
+    _lib.check(status, "isp_norm_quant")
+    return codes, scales
+
+
+def quantize_fp8(x: torch.Tensor, input_scale: float) -> torch.Tensor:
+    """``inspark_custom::fp8_quantize`` (``ops/tensorrt/cfm_gated_up_plugin.py:17-31``):
+    FP32 activation -> E4M3 codes with a static scale; the plugin's int32
+    view packs four codes per word (``codes.view(torch.int32)``)."""
+    codes, _ = norm_quant(x, kind="none", fmt="e4m3", scale=input_scale)
+    return codes
