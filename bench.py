@@ -1,0 +1,495 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quantized-linear hot path (one JSON line on rank 0).
+
+Headline workload: a Zipformer-style FM acoustic stack of
+12 W8A8 static-E4M3 layers at batch 64 x 760 frames (M = 48640 tokens),
+hidden 512.  One step = one pass of the stack over one batch:
+
+  per layer:  a   = norm_quant(x)                     RMSNorm -> E4M3        [M, 512]
+              3x  h = gemm(a,  W_ff_in)  -> E4M3 requant                     [M, 1536]
+                  y = gemm(h,  W_ff_out) -> BF16                             [M, 512]
+              qkv = gemm(a,  W_in)       -> BF16                             [M, 1536]
+              o   = gemm(a,  W_out)      -> BF16                             [M, 512]
+              c1  = gemm(a,  W_conv1)    -> E4M3 requant                     [M, 1024]
+              x'  = gemm(c1, W_conv2)    -> BF16 (next layer's input)        [M, 512]
+
+metric = GEMM TFLOP/s of the whole step (2*M*N*K summed over the 120 GEMMs);
+norm-quant and FIR GB/s are reported under "components".  Data are seeded
+synthetic tensors with BASELINE's shapes and distributions.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Multi-GPU: launched by torchrun, one rank per GPU, each rank runs its own
+B64x760 batch (weak scaling, no collective on the data path).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+M_TOKENS = 64 * 760
+HIDDEN = 512
+LAYERS = 12
+# (name, N, K, input buffer, output kind)
+LAYER_GEMMS = [
+    ("ff0_in", 1536, 512, "a", "e4m3"), ("ff0_out", 512, 1536, "h", "bf16"),
+    ("ff1_in", 1536, 512, "a", "e4m3"), ("ff1_out", 512, 1536, "h", "bf16"),
+    ("ff2_in", 1536, 512, "a", "e4m3"), ("ff2_out", 512, 1536, "h", "bf16"),
+    ("attn_in", 1536, 512, "a", "bf16"), ("attn_out", 512, 512, "a", "bf16"),
+    ("conv_in", 1024, 512, "a", "e4m3"), ("conv_out", 512, 1024, "c1", "bf16"),
+]
+DOMINANT = "attn_in"
+FLOPS_PER_TOKEN_LAYER = sum(2 * n * k for _, n, k, _, _ in LAYER_GEMMS)   # 13.63 MFLOP
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def gemm_bytes(m, n, k, out_kind):
+    out_b = 1 if out_kind == "e4m3" else 2
+    return m * k + n * k + m * n * out_b + 2 * n * 4      # A + W + C + scales/bias
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu_index), "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        rows = [r for r in csv.reader(io.StringIO(self.out or "")) if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" == r[5 + i].strip()})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# the cfg-2 stack on the GPU, as prepared C-ABI calls
+# ---------------------------------------------------------------------------
+class Stack:
+    def __init__(self, device, seed, m=M_TOKENS, layers=LAYERS):
+        import torch
+
+        from inspark_proper_format_b200 import _lib
+        self.torch = torch
+        self.lib = _lib.load()
+        self._lib = _lib
+        self.m, self.layers, self.device = m, layers, device
+        g = torch.Generator(device=device).manual_seed(seed)
+        x = torch.randn(m, HIDDEN, device=device, generator=g)
+        out_ch = torch.randperm(HIDDEN, device=device, generator=g)[:5]            # 1% outlier channels x10
+        x[:, out_ch] *= 10
+        self.x0 = x.bfloat16()
+        bf = torch.bfloat16
+        self.buf = {
+            "x_in": self.x0.clone(),                                                  # step input (never written)
+            "x": [torch.empty(m, HIDDEN, device=device, dtype=bf), torch.empty(m, HIDDEN, device=device, dtype=bf)],
+            "a": torch.empty(m, HIDDEN, device=device, dtype=torch.float8_e4m3fn),
+            "h": torch.empty(m, 1536, device=device, dtype=torch.float8_e4m3fn),
+            "c1": torch.empty(m, 1024, device=device, dtype=torch.float8_e4m3fn),
+            "y_ff": torch.empty(m, HIDDEN, device=device, dtype=bf),
+            "qkv": torch.empty(m, 1536, device=device, dtype=bf),
+            "o": torch.empty(m, HIDDEN, device=device, dtype=bf),
+        }
+        self.params = []
+        for _ in range(layers):
+            gamma = torch.rand(HIDDEN, device=device, generator=g) * 0.2 + 0.9
+            gemms = {}
+            for name, n, k, _, _ in LAYER_GEMMS:
+                w = torch.randn(n, k, device=device, generator=g) * 0.02
+                ws = (w.abs().amax(1) / 448).clamp_min(1e-12)
+                codes = (w / ws[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).contiguous()
+                bias = torch.randn(n, device=device, generator=g) * 0.01
+                gemms[name] = dict(w=codes, ws=ws.contiguous(), bias=bias.contiguous(), n=n, k=k)
+            self.params.append(dict(gamma=gamma.contiguous(), gemms=gemms))
+        self.stream = torch.cuda.current_stream(device).cuda_stream
+        self._calibrate()
+
+    # --- prepared launches -------------------------------------------------
+    def _nq_call(self, x, layer):
+        p = self.params[layer]
+        _l = self._lib
+        return (self.lib.isp_norm_quant, (x.data_ptr(), _l.BF16, self.m, HIDDEN, p["gamma"].data_ptr(), None,
+                                           1e-6, 1.0, _l.NORM_RMS_GPTFAST, _l.Q_E4M3_STATIC, p["a_scale"], None,
+                                           self.buf["a"].data_ptr(), None, self.stream), "norm_quant")
+
+    def _gemm_call(self, layer, name, n, k, src, out_kind, out_buf, a_scale, out_inv):
+        q = self.params[layer]["gemms"][name]
+        _l = self._lib
+        odt = _l.E4M3 if out_kind == "e4m3" else _l.BF16
+        return (self.lib.isp_scaled_gemm, (src.data_ptr(), q["w"].data_ptr(), _l.E4M3, self.m, n, k, a_scale, None,
+                                            q["ws"].data_ptr(), q["bias"].data_ptr(), None, _l.F32,
+                                            out_buf.data_ptr(), odt, out_inv, None, 0.0, self.stream), name)
+
+    def _layer_calls(self, layer, x_in, x_out):
+        p = self.params[layer]
+        b = self.buf
+        calls = [self._nq_call(x_in, layer)]
+        for name, n, k, src, out_kind in LAYER_GEMMS:
+            a_scale = p["a_scale"] if src == "a" else p["scale_" + src + name[:3]]
+            if out_kind == "e4m3":
+                dst = b["h"] if src == "a" and name.startswith("ff") else b["c1"]
+                inv = 1.0 / p["scale_" + ("h" if name.startswith("ff") else "c1") + name[:3]]
+            else:
+                dst = {"ff0_out": b["y_ff"], "ff1_out": b["y_ff"], "ff2_out": b["y_ff"], "attn_in": b["qkv"],
+                       "attn_out": b["o"], "conv_out": x_out}[name]
+                inv = 1.0
+            calls.append(self._gemm_call(layer, name, n, k, b[src], out_kind, dst, a_scale, inv))
+        return calls
+
+    def _io(self, layer):
+        b = self.buf
+        x_in = b["x_in"] if layer == 0 else b["x"][(layer - 1) % 2]
+        return x_in, b["x"][layer % 2]
+
+    def _calibrate(self):
+        """Seeded static calibration: activation amax/448 of every quantized GEMM input."""
+        torch = self.torch
+        b = self.buf
+        for layer in range(self.layers):
+            p = self.params[layer]
+            x_in, x_out = self._io(layer)
+            xf = x_in.float()
+            normed = (xf * torch.rsqrt(torch.mean(xf * xf, dim=-1, keepdim=True) + 1e-6)).bfloat16() * p["gamma"]
+            p["a_scale"] = float(normed.abs().amax()) / 448.0
+            fn, args, _ = self._nq_call(x_in, layer)
+            self._lib.check(fn(*args), "calibration norm_quant")
+            for name, n, k, src, out_kind in LAYER_GEMMS:
+                if out_kind != "e4m3":
+                    continue
+                q = p["gemms"][name]
+                probe = torch.empty(self.m, n, device=self.device, dtype=torch.float32)
+                from inspark_proper_format_b200.gemm import scaled_gemm
+                scaled_gemm(b["a"], q["w"], a_scale=p["a_scale"], w_scale=q["ws"], bias=q["bias"],
+                            out_dtype=torch.float32, out=probe)
+                key = "scale_" + ("h" if name.startswith("ff") else "c1") + name[:3]
+                p[key] = max(float(probe.abs().amax()) / 448.0, 1e-12)
+            # produce this layer's output (the next layer's calibration input)
+            for fn, args, _ in self._layer_calls(layer, x_in, x_out):
+                self._lib.check(fn(*args), "calibration step")
+            torch.cuda.synchronize(self.device)
+        self.calls = []
+        for layer in range(self.layers):
+            self.calls += self._layer_calls(layer, *self._io(layer))
+        self.output = self._io(self.layers - 1)[1]
+
+    def run(self, events=None):
+        """Launch one step; optionally record (start, end) events around named launches."""
+        for fn, args, name in self.calls:
+            if events is not None and name in events:
+                events[name][0].record()
+                st = fn(*args)
+                events[name][1].record()
+                events[name][2].append((events[name][0], events[name][1]))
+                events[name][0], events[name][1] = (self.torch.cuda.Event(enable_timing=True),
+                                                    self.torch.cuda.Event(enable_timing=True))
+            else:
+                st = fn(*args)
+            if st:
+                self._lib.check(st, name)
+
+    def flops(self):
+        return self.layers * self.m * FLOPS_PER_TOKEN_LAYER
+
+    def launches(self):
+        return len(self.calls)
+
+
+def fir_component(torch, device, hbm_peak):
+    """cfg-5 BigVGAN FIR, one B64 micro-batch of C=512 x T=16384 (FP32 in + out)."""
+    from inspark_proper_format_b200 import _lib
+    from inspark_proper_format_b200.alias_free import kaiser_sinc_filter, snake_inverse_beta
+    b, c, t = 64, 512, 16384
+    g = torch.Generator(device=device).manual_seed(5)
+    x = torch.randn(b, c, t, device=device, generator=g) * 0.5
+    y = torch.empty_like(x)
+    up = kaiser_sinc_filter().to(device)
+    down = up.clone()
+    alpha = torch.rand(c, device=device, generator=g) * 1.5 + 0.5
+    ib = snake_inverse_beta(alpha).contiguous()
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    args = (x.data_ptr(), b * c, c, t, up.data_ptr(), down.data_ptr(), alpha.data_ptr(), ib.data_ptr(),
+            y.data_ptr(), _lib.F32, None, 0.0, stream)
+    for _ in range(3):
+        _lib.check(lib.isp_fir_snake(*args), "fir")
+    times = []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        lib.isp_fir_snake(*args)
+        e1.record()
+        torch.cuda.synchronize(device)
+        times.append(e0.elapsed_time(e1) / 1e3)
+    sec = statistics.median(times)
+    nbytes = 8 * b * c * t
+    gbs = nbytes / sec / 1e9
+    del x, y
+    return {"workload": "BigVGAN FIR B64xC512xT16384 FP32", "us": round(sec * 1e6, 1), "GB/s": round(gbs, 1),
+            "frac_hbm": round(gbs / hbm_peak, 3), "launches": 1}
+
+
+def cpu_sample_layer(m_rows, seed=0):
+    """One cfg-2 layer of the reference's torch CPU path on m_rows tokens."""
+    import torch
+
+    from oracle.torch_path import FP8Layer
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(m_rows, HIDDEN, generator=g)
+    x[:, torch.randperm(HIDDEN, generator=g)[:5]] *= 10
+    x = x.bfloat16()
+    gamma = torch.rand(HIDDEN, generator=g) * 0.2 + 0.9
+    ws = []
+    for _, n, k, _, _ in LAYER_GEMMS:
+        w = torch.randn(n, k, generator=g) * 0.02
+        s = (w.abs().amax(1) / 448).clamp_min(1e-12)
+        ws.append((w / s[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).float() * s[:, None])
+    layer = FP8Layer(ws, [torch.tensor(0.05)] * 4)
+    norm_scale = torch.tensor(0.02)
+    flops = m_rows * FLOPS_PER_TOKEN_LAYER
+    return (lambda: layer(x, gamma, 1e-6, norm_scale)), flops
+
+
+def cpu_baseline(budget_s=12.0, m_rows=6080):
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    fn, flops = cpu_sample_layer(m_rows)
+    fn()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 2:
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return {"value": round(flops / sec / 1e12, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"one cfg-2 layer (RMSNorm, E4M3 Q/DQ, 10 FP32 F.linear on dequantized operands) on "
+                      f"{m_rows} of the {M_TOKENS} tokens, torch CPU, median of {len(times)} runs"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU PyTorch path (restated in oracle/torch_path.py)."""
+    if rank != 0:
+        return
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    m_rows = 6080
+    fn, flops = cpu_sample_layer(m_rows)
+    for _ in range(args.warmup):
+        fn()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    value = flops / sec / 1e12
+    line = {"metric": "FM-stack GEMM TFLOP/s (B64x760, W8A8 E4M3)", "value": round(value, 4), "unit": "TFLOP/s",
+            "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3", "data": "synthetic",
+            "config": {"workload": "cfg2 Zipformer FM layer sample on CPU", "tokens_per_step": m_rows,
+                       "layers_per_step": 1},
+            "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                             "kind": "port",
+                             "sample": f"one cfg-2 layer on {m_rows} tokens per step (torch CPU restatement of the "
+                                       f"reference's eager path)"},
+            "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-components", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    hbm_peak, bf16_peak, peak_kind = peaks()
+    fp8_peak = 2.0 * bf16_peak
+    stack = Stack(device, seed=1234 + rank)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)   # > 126 MB L2
+
+    for _ in range(args.warmup):
+        stack.run()
+    torch.cuda.synchronize(device)
+
+    ev = {name: [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True), []]
+          for name in (DOMINANT, "norm_quant")}
+    step_events = []
+    barrier()
+    torch.cuda.synchronize(device)
+    gpu_index = local_rank
+    if os.environ.get("CUDA_VISIBLE_DEVICES"):
+        try:
+            gpu_index = int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank])
+        except ValueError:
+            pass
+    with ClockSampler(gpu_index) as clocks:
+        for _ in range(args.steps):
+            flush.zero_()                                             # untimed L2 flush between steps
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            stack.run(events=ev)
+            e1.record()
+            step_events.append((e0, e1))
+        torch.cuda.synchronize(device)
+    barrier()
+    step_s = [a.elapsed_time(b) / 1e3 for a, b in step_events]
+    total = sum(step_s)
+    if world > 1:
+        t = torch.tensor([total], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total = float(t.item())
+    ms_per_step = total / args.steps * 1e3
+    value = world * stack.flops() * args.steps / total / 1e12
+
+    # dominant kernel roofline (attn_in: 512 -> 1536, BF16 out)
+    dom = [a.elapsed_time(b) / 1e3 for a, b in ev[DOMINANT][2]]
+    dom_s = sum(dom) / len(dom)
+    dom_bytes = gemm_bytes(stack.m, 1536, 512, "bf16")
+    dom_flops = 2 * stack.m * 1536 * 512
+    t_hbm, t_tc = dom_bytes / (hbm_peak * 1e9), dom_flops / (fp8_peak * 1e12)
+    if t_hbm >= t_tc:
+        roof = {"bound": "hbm", "achieved": round(dom_bytes / dom_s / 1e9, 1), "peak": hbm_peak, "unit": "GB/s"}
+    else:
+        roof = {"bound": "tensor", "achieved": round(dom_flops / dom_s / 1e12, 1), "peak": fp8_peak, "unit": "TFLOP/s"}
+    roof["frac"] = round(roof["achieved"] / roof["peak"], 3)
+    roof["traffic"] = None
+    roof["kernel"] = f"gemm {DOMINANT} (M={stack.m}, N=1536, K=512, E4M3 in, BF16 out), {len(dom)} launches"
+    roof["us_per_launch"] = round(dom_s * 1e6, 2)
+    roof["peak_source"] = peak_kind + (" (fp8 tensor peak = 2 x measured bf16)" if roof["bound"] == "tensor" else "")
+    nq = [a.elapsed_time(b) / 1e3 for a, b in ev["norm_quant"][2]]
+    nq_s = sum(nq) / len(nq)
+    nq_bytes = stack.m * HIDDEN * 3
+
+    # end to end through the C ABI: pinned host input -> step -> host result, every step
+    host_in = stack.x0.cpu().pin_memory()
+    host_out = torch.empty(stack.output.shape, dtype=stack.output.dtype).pin_memory()
+    e2e_s = []
+    barrier()
+    torch.cuda.synchronize(device)
+    for _ in range(max(3, args.steps // 2)):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        stack.buf["x_in"].copy_(host_in, non_blocking=True)
+        stack.run()
+        host_out.copy_(stack.output, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize(device)
+        e2e_s.append(e0.elapsed_time(e1) / 1e3)
+    e2e_total = sum(e2e_s)
+    if world > 1:
+        t = torch.tensor([e2e_total], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_total = float(t.item())
+    e2e_value = world * stack.flops() * len(e2e_s) / e2e_total / 1e12
+
+    components = {
+        "gemm_all": {"TFLOP/s": round(value / world, 1), "frac_fp8_peak": round(value / world / fp8_peak, 3)},
+        "norm_quant": {"workload": f"RMSNorm->E4M3 [{stack.m},{HIDDEN}] BF16 in", "us": round(nq_s * 1e6, 2),
+                       "GB/s": round(nq_bytes / nq_s / 1e9, 1), "frac_hbm": round(nq_bytes / nq_s / 1e9 / hbm_peak, 3)},
+    }
+    if not args.no_components and rank == 0:
+        components["fir"] = fir_component(torch, device, hbm_peak)
+
+    line = {
+        "metric": "FM-stack GEMM TFLOP/s (B64x760, W8A8 E4M3)", "value": round(value, 2), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
+        "config": {"workload": "cfg2: Zipformer-style FM stack, 12 W8A8 static-E4M3 layers, M=48640 (B64x760) "
+                               "tokens per GPU, hidden 512, fused RMSNorm->E4M3 + 10 GEMMs per layer",
+                   "tokens_per_gpu": stack.m, "layers": stack.layers, "gemm_flops_per_step": stack.flops(),
+                   "parallelism": f"dp{world} (batch sharded, no collective)",
+                   "l2": "flushed between timed steps (256 MiB write, outside the step events)"},
+        "gpu_launches": stack.launches() * args.steps,
+        "roofline": roof,
+        "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
+                "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
+        "clocks": clocks.summary(),
+        "components": components,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

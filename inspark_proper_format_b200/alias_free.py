@@ -10,9 +10,36 @@ this one keeps the high-rate row in shared memory.
 """
 from __future__ import annotations
 
+import math
+
 import torch
 
 from . import _lib
+
+
+def kaiser_sinc_filter(cutoff: float = 0.25, half_width: float = 0.3, kernel_size: int = 12) -> torch.Tensor:
+    """Kaiser-windowed sinc low-pass taps (FP32), the published design BigVGAN's
+    ``kaiser_sinc_filter1d`` uses (``.../alias_free_activation/torch/filter.py:19-42``):
+    Kaiser beta from the attenuation estimate 2.285 (N/2 - 1) pi (4 hw) + 7.95,
+    half-sample-centred taps for even lengths, unit DC gain."""
+    even = kernel_size % 2 == 0
+    half = kernel_size // 2
+    atten = 2.285 * (half - 1) * math.pi * (4 * half_width) + 7.95
+    if atten > 50.0:
+        beta = 0.1102 * (atten - 8.7)
+    elif atten >= 21.0:
+        beta = 0.5842 * (atten - 21) ** 0.4 + 0.07886 * (atten - 21.0)
+    else:
+        beta = 0.0
+    window = torch.kaiser_window(kernel_size, beta=beta, periodic=False)
+    t = (torch.arange(-half, half) + 0.5) if even else (torch.arange(kernel_size) - half)
+    taps = 2 * cutoff * window * torch.sinc(2 * cutoff * t)
+    return (taps / taps.sum()).float()
+
+
+def snake_inverse_beta(beta: torch.Tensor) -> torch.Tensor:
+    """``1 / (beta + 1e-9)`` in FP32, the Snake magnitude factor."""
+    return 1.0 / (beta.float() + 1e-9)
 
 
 def fir_snake(x: torch.Tensor, up: torch.Tensor, down: torch.Tensor, alpha: torch.Tensor,

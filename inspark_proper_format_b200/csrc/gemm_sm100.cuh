@@ -24,8 +24,21 @@ namespace gemm {
 
 constexpr int kBM = 128;
 constexpr int kBK = 128;          // bytes (= elements) of K per stage
-constexpr int kThreads = 192;
-constexpr int kEpiWarp0 = 2;
+constexpr int kEpiWarp0 = 2;      // warps 0 (TMA) and 1 (MMA) precede the epilogue warps
+
+#ifndef ISP_GEMM_STAGING_BUFS
+#define ISP_GEMM_STAGING_BUFS 1   // 32-row x 128-byte store boxes per epilogue warp
+#endif
+constexpr int kStagingBufs = ISP_GEMM_STAGING_BUFS;
+
+// 4 epilogue warps cover the 4 TMEM lane quarters once; 8 warps take two per
+// quarter, each on half of the tile's columns (twice the latency hiding).
+template <int kEpiWarps>
+struct Roles {
+  static constexpr int kEpiThreads = kEpiWarps * 32;
+  static constexpr int kThreads = 64 + kEpiThreads;
+  static constexpr int kHalves = kEpiWarps / 4;
+};
 
 enum EpiKind { EPI_SCALE = 0, EPI_SWIGLU_PAIRED = 1, EPI_SWIGLU_INTERLEAVED = 2 };
 enum OutKind { OUT_BF16 = 0, OUT_F16 = 1, OUT_F32 = 2, OUT_E4M3 = 3 };
@@ -48,14 +61,16 @@ struct Params {
   float out2_inv;
 };
 
-template <int kBN, int kStages>
+template <int kBN, int kStages, int kEpiWarps>
 struct Smem {
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = kBN * kBK;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStagingBytes = 4 * 2 * 32 * 128;  // 4 warps x 2 buffers x (32 rows x 128 B)
-  static constexpr int kBarOffset = kStages * kStageBytes + kStagingBytes;
-  static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers/flags + alignment slack
+  static constexpr int kStagingBytes = kEpiWarps * kStagingBufs * 32 * 128;  // per warp: buffers of 32 rows x 128 B
+  static constexpr int kParamOffset = kStages * kStageBytes + kStagingBytes;
+  static constexpr int kParamBytes = 512 * 4;              // per-tile column scales / bias
+  static constexpr int kBarOffset = kParamOffset + kParamBytes;
+  static constexpr int kBytes = kBarOffset + 256;          // + barriers/flags (base is 1024-aligned)
 };
 
 // ----------------------------------------------------------------------------
@@ -116,6 +131,7 @@ ISP_D void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0, in
 }
 ISP_D void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 ISP_D void bulk_wait_read_le1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+ISP_D void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 ISP_D void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 ISP_D void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 ISP_D void prefetch_tmap(const CUtensorMap* map) {
@@ -175,6 +191,27 @@ ISP_D void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 ISP_D void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Wait for outstanding tcgen05.ld and tie the loaded registers to the wait, so
+// no use of them can be scheduled before it.
+ISP_D void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+ISP_D void tmem_ld_wait(uint32_t (&r)[32], uint32_t (&s)[32]) {
+  tmem_ld_wait(r);
+  asm volatile(""
+               : "+r"(s[0]), "+r"(s[1]), "+r"(s[2]), "+r"(s[3]), "+r"(s[4]), "+r"(s[5]), "+r"(s[6]), "+r"(s[7]),
+                 "+r"(s[8]), "+r"(s[9]), "+r"(s[10]), "+r"(s[11]), "+r"(s[12]), "+r"(s[13]), "+r"(s[14]),
+                 "+r"(s[15]), "+r"(s[16]), "+r"(s[17]), "+r"(s[18]), "+r"(s[19]), "+r"(s[20]), "+r"(s[21]),
+                 "+r"(s[22]), "+r"(s[23]), "+r"(s[24]), "+r"(s[25]), "+r"(s[26]), "+r"(s[27]), "+r"(s[28]),
+                 "+r"(s[29]), "+r"(s[30]), "+r"(s[31]));
+}
 
 // ----------------------------------------------------------------------------
 // Epilogue helpers
@@ -193,9 +230,10 @@ ISP_D uint32_t pack_f16(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+// satfinite saturates +-inf and out-of-range values to +-448 and keeps NaN,
+// the same result as the reference's clamp(-448, 448) followed by the cast.
 ISP_D uint32_t pack_e4m3x4(float a, float b, float c, float d) {
-  return static_cast<uint32_t>(e4m3x2(clamp448(a), clamp448(b))) |
-         (static_cast<uint32_t>(e4m3x2(clamp448(c), clamp448(d))) << 16);
+  return static_cast<uint32_t>(e4m3x2(a, b)) | (static_cast<uint32_t>(e4m3x2(c, d)) << 16);
 }
 
 // Write one thread's 128-byte row of the 32 x 128 B staging box (128-byte swizzle).
@@ -220,18 +258,198 @@ ISP_D float silu_mul(float g, float u) {
   return __fmul_rn(__fmul_rn(g, sig), u);
 }
 
+// Named barrier among the epilogue warps only (id 1).
+template <int kEpiThreads>
+ISP_D void epilogue_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
+
+ISP_D void lds32(const float* p, float (&v)[32]) {   // uniform address: a broadcast read
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 t = *reinterpret_cast<const float4*>(p + 4 * j);
+    v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+  }
+}
+
+// Shared layout of the per-tile parameters (512 floats), filled from registers
+// fetched one tile ahead so the L2 latency is off the critical path:
+//   EPI_SCALE:              [0, BN) w_scale (1 when absent), [256, 256 + BN) bias (0 when absent)
+//   EPI_SWIGLU_PAIRED:      [0, 128) s1, [128, 256) s3
+//   EPI_SWIGLU_INTERLEAVED: [0, 256) S[2 n0 ...] (gate, up alternating)
+// Columns at or past N read as 0, so the math needs no column guards.
+// For EPI_SCALE with a per-tensor activation scale the staged column scale is
+// already sa * w_scale[n] (the product the INT8 reference forms as AS * WS[n]).
+template <int kEpi, int kBN, int kEpiThreads>
+struct TileParams {
+  static constexpr int kPer = 256 / kEpiThreads;
+  float a[kPer], b[kPer];   // entries et + kEpiThreads * h of the 256-wide shared arrays
+
+  ISP_D void fetch(const Params& p, int n0, int et) {
+#pragma unroll
+    for (int h = 0; h < kPer; ++h) {
+      const int i = et + kEpiThreads * h;
+      float x = 0.f, y = 0.f;
+      if constexpr (kEpi == EPI_SCALE) {
+        const int n = n0 + i;
+        if (i < kBN && n < p.N) {
+          x = p.w_scale != nullptr ? __ldg(p.w_scale + n) : 1.f;
+          if (p.a_scale_rows == nullptr) x = __fmul_rn(p.a_scale, x);
+          y = p.bias != nullptr ? __ldg(p.bias + n) : 0.f;
+        }
+      } else if constexpr (kEpi == EPI_SWIGLU_PAIRED) {
+        const int n = n0 + (i & 127);
+        if (n < p.N) x = __ldg((i < 128 ? p.w_scale : p.w_scale2) + n);
+      } else {
+        if (n0 + (i >> 1) < p.N) x = __ldg(p.w_scale + 2 * n0 + i);
+      }
+      a[h] = x;
+      b[h] = y;
+    }
+  }
+  ISP_D void store(float* sp, int et) const {
+#pragma unroll
+    for (int h = 0; h < kPer; ++h) {
+      sp[et + kEpiThreads * h] = a[h];
+      sp[256 + et + kEpiThreads * h] = b[h];
+    }
+  }
+};
+
+// Issue the TMEM loads of output group g (32 output columns).
+template <int kEpi, int kBN>
+ISP_D void tmem_load_group(uint32_t t_row, int g, uint32_t (&a)[32], uint32_t (&b)[32]) {
+  if constexpr (kEpi == EPI_SCALE) {
+    tmem_ld32(t_row + g * 32, a);
+  } else if constexpr (kEpi == EPI_SWIGLU_PAIRED) {
+    tmem_ld32(t_row + g * 32, a);                // gate
+    tmem_ld32(t_row + kBN / 2 + g * 32, b);      // up
+  } else {
+    tmem_ld32(t_row + g * 64, a);                // (gate, up) pairs of outputs 32g .. 32g+15
+    tmem_ld32(t_row + g * 64 + 32, b);           // outputs 32g+16 .. 32g+31
+  }
+}
+
+// kRows (per-row activation scale sa):
+//   FP8  v = fma(acc * sa, ws[n], bias[n])        (ops/triton/fp8.py:32-33 order)
+//   INT8 v = (acc * (sa * ws[n])) + bias[n]
+// otherwise the staged scale c[n] already holds sa * ws[n]:
+//   FP8  v = fma(acc, c[n], bias[n]);  INT8 v = (acc * c[n]) + bias[n]
+// (INT8 keeps separate roundings, as i8_residual_runtime_kernel.py:18-20).
+template <bool kInt8, bool kRows>
+ISP_D void scale_group(const uint32_t (&r)[32], float sa, const float* ws_s, const float* bs_s, float (&v)[32]) {
+  float ws[32], bs[32];
+  lds32(ws_s, ws);
+  lds32(bs_s, bs);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if constexpr (kInt8) {
+      const float c = kRows ? __fmul_rn(sa, ws[j]) : ws[j];
+      v[j] = __fadd_rn(__fmul_rn(acc_value<true>(r[j]), c), bs[j]);
+    } else {
+      const float a = kRows ? __fmul_rn(acc_value<false>(r[j]), sa) : acc_value<false>(r[j]);
+      v[j] = __fmaf_rn(a, ws[j], bs[j]);
+    }
+  }
+}
+
+ISP_D void add_residual(const Params& p, int m, int n, float (&v)[32]) {
+  const int64_t off = static_cast<int64_t>(m) * p.N + n;
+  if (n + 32 <= p.N) {
+    if (p.residual_f32) {
+      float r[32];
+      load_f32x32(static_cast<const float*>(p.residual) + off, r);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], r[j]);
+    } else {
+      const uint4* q = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.residual) + off);
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float f[8];
+        bf16x8_to_f32(__ldg(q + h), f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[8 * h + j] = __fadd_rn(v[8 * h + j], f[j]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (n + j < p.N) {
+        const float r = p.residual_f32 ? __ldg(static_cast<const float*>(p.residual) + off + j)
+                                       : __bfloat162float(static_cast<const __nv_bfloat16*>(p.residual)[off + j]);
+        v[j] = __fadd_rn(v[j], r);
+      }
+    }
+  }
+}
+
+ISP_D void store_dual_e4m3(const Params& p, int m, int n, const float (&v)[32]) {
+  uint8_t* o2 = static_cast<uint8_t*>(p.out2) + static_cast<int64_t>(m) * p.N + n;
+  uint32_t q[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    q[j] = pack_e4m3x4(__fmul_rn(v[4 * j], p.out2_inv), __fmul_rn(v[4 * j + 1], p.out2_inv),
+                       __fmul_rn(v[4 * j + 2], p.out2_inv), __fmul_rn(v[4 * j + 3], p.out2_inv));
+  if (n + 32 <= p.N) {
+    reinterpret_cast<uint4*>(o2)[0] = make_uint4(q[0], q[1], q[2], q[3]);
+    reinterpret_cast<uint4*>(o2)[1] = make_uint4(q[4], q[5], q[6], q[7]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n + j < p.N) o2[j] = static_cast<uint8_t>(q[j >> 2] >> (8 * (j & 3)));
+  }
+}
+
+// SwiGLU of output group g: h = silu(acc_g * s_g) * (acc_u * s_u), then
+// clamp(h * out_inv) (E4M3 codes follow) or its E4M3 round trip * out_scale.
+template <int kEpi, int kOut>
+ISP_D void swiglu_group(const uint32_t (&a)[32], const uint32_t (&b)[32], const float* sp, int g, float out_inv,
+                        float out_scale, float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float gacc, uacc, sg, su;
+    if constexpr (kEpi == EPI_SWIGLU_PAIRED) {
+      gacc = __uint_as_float(a[j]);
+      uacc = __uint_as_float(b[j]);
+      sg = sp[g * 32 + j];
+      su = sp[128 + g * 32 + j];
+    } else {
+      const uint32_t(&src)[32] = j < 16 ? a : b;
+      const int c = 2 * (j & 15);
+      gacc = __uint_as_float(src[c]);
+      uacc = __uint_as_float(src[c + 1]);
+      sg = sp[g * 64 + 2 * j];
+      su = sp[g * 64 + 2 * j + 1];
+    }
+    v[j] = __fmul_rn(silu_mul(__fmul_rn(gacc, sg), __fmul_rn(uacc, su)), out_inv);
+  }
+  if constexpr (kOut == OUT_F32) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      const uint16_t q2 = e4m3x2(v[j], v[j + 1]);
+      v[j] = __fmul_rn(e4m3_to_f32(static_cast<uint8_t>(q2 & 0xFF)), out_scale);
+      v[j + 1] = __fmul_rn(e4m3_to_f32(static_cast<uint8_t>(q2 >> 8)), out_scale);
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------
 // The kernel
 // ----------------------------------------------------------------------------
-template <int kBN, int kStages, bool kInt8, int kEpi, int kOut>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int kBN, int kStages, int kEpiWarps, bool kInt8, int kEpi, int kOut>
+__global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_out,
                 const Params p) {
-  using L = Smem<kBN, kStages>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using L = Smem<kBN, kStages, kEpiWarps>;
+  using R = Roles<kEpiWarps>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // The 128-byte swizzle patterns assume a 1024-byte aligned base; refuse to run otherwise.
+  if ((smem_u32(smem_raw) & 1023u) != 0) {
+    if (threadIdx.x == 0) atomicExch(&g_device_error, (int)ISP_ERR_ALIGN);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   uint8_t* staging = smem + kStages * L::kStageBytes;
+  float* params = reinterpret_cast<float*>(smem + L::kParamOffset);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* empty_bar = full_bar + kStages;
   uint64_t* tfull_bar = empty_bar + kStages;     // [2]
@@ -251,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);              // one arrive per epilogue warp
+      mbar_init(&tempty_bar[a], kEpiWarps);      // one arrive per epilogue warp
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -347,18 +565,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - kEpiWarp0;             // 0..3
+    const int ew = warp - kEpiWarp0;             // 0 .. kEpiWarps-1
+    const int et = threadIdx.x - kEpiWarp0 * 32; // 0 .. kEpiThreads-1
     const int quarter = warp & 3;                // TMEM lane quarter this warp may access
+    const int half = ew / 4;                     // which share of the columns (8-warp epilogue)
     const int row_in_tile = quarter * 32 + lane;
-    uint8_t* stage_base = staging + ew * (2 * 32 * 128);
+    uint8_t* stage_base = staging + ew * (kStagingBufs * 32 * 128);
     int sbuf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     constexpr int kOutCols = (kEpi == EPI_SCALE) ? kBN : kBN / 2;
     constexpr int kChunkCols = 128 / (kOut == OUT_F32 ? 4 : (kOut == OUT_E4M3 ? 1 : 2));
+    constexpr int kGroupsPerChunk = kChunkCols / 32;
+    constexpr int kGroups = kOutCols / 32 / R::kHalves;   // 32-column groups this warp handles
+    static_assert(kGroups % kGroupsPerChunk == 0, "a warp's columns must be whole store boxes");
+    const int g0 = half * kGroups;
+    constexpr int kWordsPerGroup = 32 / kGroupsPerChunk;
+    TileParams<kEpi, kBN, R::kEpiThreads> tp;
+    if (blockIdx.x < total_tiles) tp.fetch(p, (blockIdx.x % p.n_tiles) * kOutCols, et);
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       const int m0 = (tile / p.n_tiles) * kBM;
       const int n0 = (tile % p.n_tiles) * kOutCols;
+      // Per-column parameters of this tile -> shared memory (zero past column N),
+      // then start fetching the next tile's.
+      epilogue_sync<R::kEpiThreads>();
+      tp.store(params, et);
+      epilogue_sync<R::kEpiThreads>();
+      const int next = tile + gridDim.x;
+      if (next < total_tiles) tp.fetch(p, (next % p.n_tiles) * kOutCols, et);
       if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
       const int m = m0 + row_in_tile;
@@ -367,155 +601,77 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.a_scale_rows != nullptr && row_ok) sa = __ldg(p.a_scale_rows + m);
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
 
-#pragma unroll 1
-      for (int c0 = 0; c0 < kOutCols; c0 += kChunkCols) {
-        uint32_t w[32];
+      uint32_t ca[32], cb[32];
+      tmem_load_group<kEpi, kBN>(t_row, g0, ca, cb);
+      uint32_t w[32];
 #pragma unroll
-        for (int sub = 0; sub < kChunkCols / 32; ++sub) {
-          const int col = c0 + sub * 32;         // first output column of these 32, tile-relative
-          const int n = n0 + col;                // global output column
-          float v[32];
-          if constexpr (kEpi == EPI_SCALE) {
-            uint32_t r[32];
-            tmem_ld32(t_row + col, r);
-            tmem_ld_wait();
-            float ws[32], bs[32];
-            const bool cols_ok = n + 32 <= p.N;
-            if (p.w_scale != nullptr && cols_ok) load_f32x32(p.w_scale + n, ws);
-            if (p.bias != nullptr && cols_ok) load_f32x32(p.bias + n, bs);
+      for (int g = 0; g < kGroups; ++g) {
+        if constexpr (kEpi == EPI_SCALE) tmem_ld_wait(ca);
+        else tmem_ld_wait(ca, cb);
+        uint32_t na[32], nb[32];
+        if (g + 1 < kGroups) {
+          tmem_load_group<kEpi, kBN>(t_row, g0 + g + 1, na, nb);    // overlaps this group's math
+        } else {
+          // every column of the accumulator is in registers: hand it back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        }
+        const int col = (g0 + g) * 32;           // first output column of this group, tile-relative
+        const int n = n0 + col;
+        float v[32];
+        if constexpr (kEpi == EPI_SCALE) {
+          if (p.a_scale_rows != nullptr) scale_group<kInt8, true>(ca, sa, params + col, params + 256 + col, v);
+          else scale_group<kInt8, false>(ca, sa, params + col, params + 256 + col, v);
+          if (p.residual != nullptr && row_ok) add_residual(p, m, n, v);
+          if (p.out2 != nullptr && row_ok) store_dual_e4m3(p, m, n, v);
+          if constexpr (kOut == OUT_E4M3) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              // FP8: (acc * sa) * ws[n] (ops/triton/fp8.py:32); INT8: acc * (AS * WS[n])
-              // (i8_residual_runtime_kernel.py:18-20).  The order decides the rounding.
-              float t;
-              if (p.w_scale != nullptr) {
-                const float wsj = cols_ok ? ws[j] : (n + j < p.N ? __ldg(p.w_scale + n + j) : 0.f);
-                t = kInt8 ? __fmul_rn(acc_value<kInt8>(r[j]), __fmul_rn(sa, wsj))
-                          : __fmul_rn(__fmul_rn(acc_value<kInt8>(r[j]), sa), wsj);
-              } else {
-                t = __fmul_rn(acc_value<kInt8>(r[j]), sa);
-              }
-              if (p.bias != nullptr) t = __fadd_rn(t, cols_ok ? bs[j] : (n + j < p.N ? __ldg(p.bias + n + j) : 0.f));
-              v[j] = t;
-            }
-            if (p.residual != nullptr && row_ok) {
-              if (p.residual_f32) {
-                const float* rr = static_cast<const float*>(p.residual) + static_cast<int64_t>(m) * p.N + n;
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (n + j < p.N) v[j] = __fadd_rn(v[j], __ldg(rr + j));
-              } else {
-                const __nv_bfloat16* rr = static_cast<const __nv_bfloat16*>(p.residual) + static_cast<int64_t>(m) * p.N + n;
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (n + j < p.N) v[j] = __fadd_rn(v[j], __bfloat162float(rr[j]));
-              }
-            }
-            if (p.out2 != nullptr && row_ok) {
-              uint8_t* o2 = static_cast<uint8_t*>(p.out2) + static_cast<int64_t>(m) * p.N + n;
-              uint32_t q[8];
-#pragma unroll
-              for (int j = 0; j < 8; ++j)
-                q[j] = pack_e4m3x4(__fmul_rn(v[4 * j], p.out2_inv), __fmul_rn(v[4 * j + 1], p.out2_inv),
-                                   __fmul_rn(v[4 * j + 2], p.out2_inv), __fmul_rn(v[4 * j + 3], p.out2_inv));
-              if (n + 32 <= p.N) {
-                reinterpret_cast<uint4*>(o2)[0] = make_uint4(q[0], q[1], q[2], q[3]);
-                reinterpret_cast<uint4*>(o2)[1] = make_uint4(q[4], q[5], q[6], q[7]);
-              } else {
-                for (int j = 0; j < 32 && n + j < p.N; ++j) o2[j] = static_cast<uint8_t>(q[j >> 2] >> (8 * (j & 3)));
-              }
-            }
-          } else {
-            // SwiGLU: gate/up accumulator columns for output columns col..col+31
-            uint32_t g[32], u[32];
-            float s_g[32], s_u[32];
-            if constexpr (kEpi == EPI_SWIGLU_PAIRED) {
-              tmem_ld32(t_row + col, g);
-              tmem_ld32(t_row + kBN / 2 + col, u);
-              tmem_ld_wait();
-              if (n < p.N) {                    // N % 32 == 0: a 32-column group is all in or all out
-                load_f32x32(p.w_scale + n, s_g);
-                load_f32x32(p.w_scale2 + n, s_u);
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) s_g[j] = s_u[j] = 0.f;
-              }
-            } else {
-              uint32_t lo[32], hi[32];
-              tmem_ld32(t_row + 2 * col, lo);
-              tmem_ld32(t_row + 2 * col + 32, hi);
-              tmem_ld_wait();
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                g[j] = lo[2 * j]; u[j] = lo[2 * j + 1];
-                g[16 + j] = hi[2 * j]; u[16 + j] = hi[2 * j + 1];
-              }
-              float sl[32], sh[32];
-              if (n < p.N) {
-                load_f32x32(p.w_scale + 2 * n, sl);
-                load_f32x32(p.w_scale + 2 * n + 32, sh);
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) sl[j] = sh[j] = 0.f;
-              }
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                s_g[j] = sl[2 * j]; s_u[j] = sl[2 * j + 1];
-                s_g[16 + j] = sh[2 * j]; s_u[16 + j] = sh[2 * j + 1];
-              }
-            }
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float gv = __fmul_rn(__uint_as_float(g[j]), s_g[j]);
-              const float uv = __fmul_rn(__uint_as_float(u[j]), s_u[j]);
-              v[j] = clamp448(__fmul_rn(silu_mul(gv, uv), p.out_inv));
-            }
-            if constexpr (kOut == OUT_F32) {
-              // DEQUANT: e4m3 round trip times the output scale
-#pragma unroll
-              for (int j = 0; j < 32; j += 2) {
-                const uint16_t q2 = e4m3x2(v[j], v[j + 1]);
-                v[j] = __fmul_rn(e4m3_to_f32(static_cast<uint8_t>(q2 & 0xFF)), p.out_scale);
-                v[j + 1] = __fmul_rn(e4m3_to_f32(static_cast<uint8_t>(q2 >> 8)), p.out_scale);
-              }
-            }
+            for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(v[j], p.out_inv);
           }
-          // ---- convert this sub-block into its words of the 128-byte row
-          if constexpr (kOut == OUT_F32) {
+        } else {
+          swiglu_group<kEpi, kOut>(ca, cb, params, g0 + g, p.out_inv, p.out_scale, v);
+        }
+        const int wo = (g % kGroupsPerChunk) * kWordsPerGroup;
+        if constexpr (kOut == OUT_F32) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
-          } else if constexpr (kOut == OUT_BF16) {
+          for (int j = 0; j < 32; ++j) w[wo + j] = __float_as_uint(v[j]);
+        } else if constexpr (kOut == OUT_BF16) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) w[sub * 16 + j] = pack_bf16(v[2 * j], v[2 * j + 1]);
-          } else if constexpr (kOut == OUT_F16) {
+          for (int j = 0; j < 16; ++j) w[wo + j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+        } else if constexpr (kOut == OUT_F16) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) w[sub * 16 + j] = pack_f16(v[2 * j], v[2 * j + 1]);
-          } else {  // OUT_E4M3
-            if constexpr (kEpi == EPI_SCALE) {
+          for (int j = 0; j < 16; ++j) w[wo + j] = pack_f16(v[2 * j], v[2 * j + 1]);
+        } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(v[j], p.out_inv);
-            }
+          for (int j = 0; j < 8; ++j) w[wo + j] = pack_e4m3x4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        if (g % kGroupsPerChunk == kGroupsPerChunk - 1) {
+          // ---- stage + TMA store of the 32-row x 128-byte box
+          const int c0 = col - (kGroupsPerChunk - 1) * 32;
+          uint8_t* st = stage_base + sbuf * (32 * 128);
+          if (lane == 0) {                       // the store that last used this buffer has read it
+            if constexpr (kStagingBufs == 2) bulk_wait_read_le1();
+            else bulk_wait_read_all();
+          }
+          __syncwarp();
+          stage_row(st, lane, w);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && m0 + quarter * 32 < p.M) {   // boxes wholly below row M are skipped
+            tma_store_2d(&tm_out, st, n0 + c0, m0 + quarter * 32);
+            bulk_commit();
+          }
+          if constexpr (kStagingBufs == 2) sbuf ^= 1;
+        }
+        if (g + 1 < kGroups) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) w[sub * 8 + j] = pack_e4m3x4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          for (int j = 0; j < 32; ++j) {
+            ca[j] = na[j];
+            cb[j] = nb[j];
           }
         }
-        // ---- stage + TMA store of the 32-row x 128-byte box
-        uint8_t* st = stage_base + sbuf * (32 * 128);
-        if (lane == 0) bulk_wait_read_le1();     // the store that last used this buffer has read it
-        __syncwarp();
-        stage_row(st, lane, w);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && m0 + quarter * 32 < p.M) {   // boxes wholly below row M are skipped
-          tma_store_2d(&tm_out, st, n0 + c0, m0 + quarter * 32);
-          bulk_commit();
-        }
-        sbuf ^= 1;
       }
-      // accumulator fully read: hand it back to the MMA warp
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
     if (lane == 0) bulk_wait_all();

@@ -86,11 +86,23 @@ bool make_out_map(CUtensorMap* map, void* out, int out_kind, int64_t M, int N) {
                   static_cast<uint32_t>(128 / eb), 32);
 }
 
-template <int kBN, int kStages, bool kInt8, int kEpi, int kOut>
+#ifndef ISP_GEMM_STAGES
+#define ISP_GEMM_STAGES 4
+#endif
+#ifndef ISP_GEMM_SCALE_EPI_WARPS
+#define ISP_GEMM_SCALE_EPI_WARPS 8
+#endif
+constexpr int kBN = 256;
+constexpr int kStages = ISP_GEMM_STAGES;
+constexpr int kScaleEpiWarps = ISP_GEMM_SCALE_EPI_WARPS;   // scale/bias/residual epilogues
+constexpr int kSwigluEpiWarps = 4;                         // SwiGLU: 128 output columns per tile
+
+template <int kBN, int kStages, int kEpiWarps, bool kInt8, int kEpi, int kOut>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, const CUtensorMap& o,
            const Params& p, cudaStream_t stream) {
-  auto kern = gemm_kernel<kBN, kStages, kInt8, kEpi, kOut>;
-  constexpr int kSmem = Smem<kBN, kStages>::kBytes;
+  auto kern = gemm_kernel<kBN, kStages, kEpiWarps, kInt8, kEpi, kOut>;
+  constexpr int kSmem = Smem<kBN, kStages, kEpiWarps>::kBytes;
+  static_assert(kSmem <= 232448, "shared memory budget of one sm_100 CTA");
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -101,21 +113,18 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, co
   }
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, kThreads, kSmem, stream>>>(a, b, b2, o, p);
+  kern<<<grid, Roles<kEpiWarps>::kThreads, kSmem, stream>>>(a, b, b2, o, p);
   return launch_status();
 }
-
-constexpr int kBN = 256;
-constexpr int kStages = 4;
 
 template <bool kInt8>
 int dispatch_scale_out(int out_kind, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
                        const Params& p, cudaStream_t s) {
   switch (out_kind) {
-    case OUT_BF16: return launch<kBN, kStages, kInt8, EPI_SCALE, OUT_BF16>(a, b, b, o, p, s);
-    case OUT_F16: return launch<kBN, kStages, kInt8, EPI_SCALE, OUT_F16>(a, b, b, o, p, s);
-    case OUT_F32: return launch<kBN, kStages, kInt8, EPI_SCALE, OUT_F32>(a, b, b, o, p, s);
-    case OUT_E4M3: return launch<kBN, kStages, kInt8, EPI_SCALE, OUT_E4M3>(a, b, b, o, p, s);
+    case OUT_BF16: return launch<kBN, kStages, kScaleEpiWarps, kInt8, EPI_SCALE, OUT_BF16>(a, b, b, o, p, s);
+    case OUT_F16: return launch<kBN, kStages, kScaleEpiWarps, kInt8, EPI_SCALE, OUT_F16>(a, b, b, o, p, s);
+    case OUT_F32: return launch<kBN, kStages, kScaleEpiWarps, kInt8, EPI_SCALE, OUT_F32>(a, b, b, o, p, s);
+    case OUT_E4M3: return launch<kBN, kStages, kScaleEpiWarps, kInt8, EPI_SCALE, OUT_E4M3>(a, b, b, o, p, s);
     default: return ISP_ERR_DTYPE;
   }
 }
@@ -293,11 +302,11 @@ int isp_gated_up(const void* A, const void* W1, const void* W3, int interleaved,
   p.out_scale = out_scale;
   if (interleaved) {
     return out_kind == OUT_E4M3
-               ? launch<kBN, kStages, false, EPI_SWIGLU_INTERLEAVED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
-               : launch<kBN, kStages, false, EPI_SWIGLU_INTERLEAVED, OUT_F32>(ta, tb, tb2, to, p, stream);
+               ? launch<kBN, kStages, kSwigluEpiWarps, false, EPI_SWIGLU_INTERLEAVED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
+               : launch<kBN, kStages, kSwigluEpiWarps, false, EPI_SWIGLU_INTERLEAVED, OUT_F32>(ta, tb, tb2, to, p, stream);
   }
-  return out_kind == OUT_E4M3 ? launch<kBN, kStages, false, EPI_SWIGLU_PAIRED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
-                              : launch<kBN, kStages, false, EPI_SWIGLU_PAIRED, OUT_F32>(ta, tb, tb2, to, p, stream);
+  return out_kind == OUT_E4M3 ? launch<kBN, kStages, kSwigluEpiWarps, false, EPI_SWIGLU_PAIRED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
+                              : launch<kBN, kStages, kSwigluEpiWarps, false, EPI_SWIGLU_PAIRED, OUT_F32>(ta, tb, tb2, to, p, stream);
 }
 
 }  // extern "C"

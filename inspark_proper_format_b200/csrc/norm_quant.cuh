@@ -149,8 +149,9 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const float* q = &v[i][4 * h];
-          uint32_t lo = e4m3x2(clamp448(__fdiv_rn(q[0], s)), clamp448(__fdiv_rn(q[1], s)));
-          uint32_t hi = e4m3x2(clamp448(__fdiv_rn(q[2], s)), clamp448(__fdiv_rn(q[3], s)));
+          // satfinite == the reference's clamp(-448, 448) before the cast (NaN stays NaN)
+          uint32_t lo = e4m3x2(__fdiv_rn(q[0], s), __fdiv_rn(q[1], s));
+          uint32_t hi = e4m3x2(__fdiv_rn(q[2], s), __fdiv_rn(q[3], s));
           w[h] = lo | (hi << 16);
         }
         *reinterpret_cast<uint2*>(out + g * 8) = make_uint2(w[0], w[1]);

@@ -13,6 +13,8 @@ Reference surfaces mirrored here:
 """
 from __future__ import annotations
 
+import weakref
+
 import torch
 
 from . import _lib
@@ -132,14 +134,18 @@ _CANONICAL: dict = {}
 def canonical_weight(packed: torch.Tensor, n: int) -> torch.Tensor:
     """[K, Npad] reference packing -> the K-major [N, K] operand tcgen05 reads.
 
-    The transpose is done once per packed tensor and cached (weights are
-    immutable after ``prepare``)."""
-    key = (packed.data_ptr(), tuple(packed.shape), n, packed.device)
+    The transpose is done once per packed tensor object and cached; the entry
+    is keyed by object identity and invalidated when the tensor is freed or
+    modified in place (its version counter changes)."""
+    key = (id(packed), n)
     hit = _CANONICAL.get(key)
-    if hit is None:
-        hit = packed[:, :n].t().contiguous()
-        _CANONICAL[key] = hit
-    return hit
+    if hit is not None:
+        ref, version, canon = hit
+        if ref() is packed and version == packed._version:
+            return canon
+    canon = packed[:, :n].t().contiguous()
+    _CANONICAL[key] = (weakref.ref(packed, lambda _r, k=key: _CANONICAL.pop(k, None)), packed._version, canon)
+    return canon
 
 
 def linear(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, bias: torch.Tensor | None = None,
