@@ -250,13 +250,15 @@ def fir_component(torch, device, hbm_peak):
     g = torch.Generator(device=device).manual_seed(5)
     x = torch.randn(b, c, t, device=device, generator=g) * 0.5
     y = torch.empty_like(x)
-    up = kaiser_sinc_filter().to(device)
-    down = up.clone()
+    from inspark_proper_format_b200.alias_free import host_taps
+    up = host_taps(kaiser_sinc_filter())
+    down = host_taps(kaiser_sinc_filter())
     alpha = torch.rand(c, device=device, generator=g) * 1.5 + 0.5
     ib = snake_inverse_beta(alpha).contiguous()
     lib = _lib.load()
     stream = torch.cuda.current_stream(device).cuda_stream
-    args = (x.data_ptr(), b * c, c, t, up.data_ptr(), down.data_ptr(), alpha.data_ptr(), ib.data_ptr(),
+    import ctypes
+    args = (x.data_ptr(), b * c, c, t, ctypes.addressof(up), ctypes.addressof(down), alpha.data_ptr(), ib.data_ptr(),
             y.data_ptr(), _lib.F32, None, 0.0, stream)
     for _ in range(3):
         _lib.check(lib.isp_fir_snake(*args), "fir")

@@ -113,9 +113,12 @@ int isp_norm_quant(const void *x, int x_dtype, int64_t M, int K,
  *   inspark_custom::small_fir_activation[_tiled]  ops/tensorrt/vocoder_tiled_fir_plugin.py:11-36
  *   inspark_custom::small_fir_activation_quantized  deployment/multibatch/fir_quant_plugin.py:11-26
  *
- * x: [rows, T] FP32 with rows = B*C and channel = row % C.
- * up, down: 12 FP32 taps each.  alpha, inv_beta: [C] FP32 (linear alpha;
- * inv_beta = 1/(beta + 1e-9)).
+ * x: [rows, T] FP32 with rows = B*C and channel = row % C; 16-byte aligned
+ *    (rows with T % 4 == 0 are streamed by bulk async copies).
+ * up, down: 12 FP32 taps each, in HOST memory (model constants; they are
+ *   passed by value to the kernel so every FMA reads them from the constant
+ *   bank).  alpha, inv_beta: [C] FP32 on the device (linear alpha;
+ *   inv_beta = 1/(beta + 1e-9)).
  * out_dtype ISP_F32: y [rows, T] FP32.
  * out_dtype ISP_I8: y = clamp(rint((v / smooth[c]) / scale), -128, 127) int8.
  */

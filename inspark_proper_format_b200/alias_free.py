@@ -10,11 +10,29 @@ this one keeps the high-rate row in shared memory.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
 
 from . import _lib
+
+_Taps = ctypes.c_float * 12
+
+
+def host_taps(filt) -> "ctypes.Array":
+    """12 FIR taps as a host array for the C ABI (the taps travel by value to
+    the kernel).  Accepts a tensor on any device, a numpy array or a sequence;
+    a CUDA tensor costs one device-to-host copy, so modules convert once."""
+    if isinstance(filt, _Taps):
+        return filt
+    if isinstance(filt, torch.Tensor):
+        values = filt.detach().float().reshape(-1).cpu().tolist()
+    else:
+        values = [float(v) for v in (filt.reshape(-1) if hasattr(filt, "reshape") else filt)]
+    if len(values) != 12:
+        raise ValueError("Tiled FIR requires complete 12-tap filters")
+    return _Taps(*values)
 
 
 def kaiser_sinc_filter(cutoff: float = 0.25, half_width: float = 0.3, kernel_size: int = 12) -> torch.Tensor:
@@ -42,17 +60,20 @@ def snake_inverse_beta(beta: torch.Tensor) -> torch.Tensor:
     return 1.0 / (beta.float() + 1e-9)
 
 
-def fir_snake(x: torch.Tensor, up: torch.Tensor, down: torch.Tensor, alpha: torch.Tensor,
+def fir_snake(x: torch.Tensor, up, down, alpha: torch.Tensor,
               inverse_beta: torch.Tensor, out: torch.Tensor | None = None,
               smooth: torch.Tensor | None = None, scale: float | None = None) -> torch.Tensor:
     """y = down-FIR(Snake(up-FIR(x))) on contiguous CUDA FP32 [B, C, T].
 
-    With ``smooth``/``scale`` the output is the INT8 SmoothQuant code of y.
+    ``up``/``down``: 12 taps (tensor on any device, sequence, or a
+    ``host_taps`` array).  With ``smooth``/``scale`` the output is the INT8
+    SmoothQuant code of y.
     """
     if x.ndim != 3 or x.dtype != torch.float32 or not x.is_cuda or not x.is_contiguous():
         raise ValueError("Tiled FIR expects contiguous CUDA FP32 B,C,F")
     b, c, t = x.shape
-    for name, v, n in (("up", up, 12), ("down", down, 12), ("alpha", alpha, c), ("inverse_beta", inverse_beta, c)):
+    up, down = host_taps(up), host_taps(down)
+    for name, v, n in (("alpha", alpha, c), ("inverse_beta", inverse_beta, c)):
         if v.numel() != n or v.dtype != torch.float32 or not v.is_cuda or not v.is_contiguous():
             raise ValueError(f"Tiled FIR channel/length mismatch ({name})")
     quant = smooth is not None
@@ -62,7 +83,7 @@ def fir_snake(x: torch.Tensor, up: torch.Tensor, down: torch.Tensor, alpha: torc
     if out is None:
         out = torch.empty(x.shape, device=x.device, dtype=torch.int8 if quant else torch.float32)
     status = _lib.load().isp_fir_snake(
-        x.data_ptr(), b * c, c, t, up.data_ptr(), down.data_ptr(), alpha.data_ptr(), inverse_beta.data_ptr(),
+        x.data_ptr(), b * c, c, t, ctypes.addressof(up), ctypes.addressof(down), alpha.data_ptr(), inverse_beta.data_ptr(),
         out.data_ptr(), _lib.I8 if quant else _lib.F32, _lib.ptr(smooth), float(scale or 0.0),
         _lib.stream_handle(x.device))
     _lib.check(status, "isp_fir_snake")
@@ -90,11 +111,12 @@ class FusedAliasFree(torch.nn.Module):
         self.register_buffer("inverse_beta", (1.0 / (beta + 1e-9)).contiguous())
         self.register_buffer("up", _filter(original.upsample.filter))
         self.register_buffer("down", _filter(original.downsample.lowpass.filter))
+        self._taps = (host_taps(self.up), host_taps(self.down))
 
     def forward(self, x):
         if x.dtype != torch.float32:
             raise ValueError("Only tested FP32 activation interface")
-        return fir_snake(x.contiguous(), self.up, self.down, self.alpha, self.inverse_beta)
+        return fir_snake(x.contiguous(), *self._taps, self.alpha, self.inverse_beta)
 
 
 def install(vocoder):
@@ -131,7 +153,7 @@ class TiledFIR:
             raise ValueError("Unsupported tiled FIR schedule")
         if up.numel() != 12 or down.numel() != 12:
             raise ValueError("Tiled FIR requires complete 12-tap filters")
-        self.parameters = (_filter(up), _filter(down), *_linear_params(alpha, beta))
+        self.parameters = (host_taps(up), host_taps(down), *_linear_params(alpha, beta))
         self.block, self.warps = block, warps
         self.output = None
 
@@ -152,7 +174,7 @@ class SmallFIR:
     """``ops/triton/vocoder_small_fir.py:31-40`` surface (rows up to 4096 samples)."""
 
     def __init__(self, up, down, alpha, beta):
-        self.parameters = (_filter(up), _filter(down), *_linear_params(alpha, beta))
+        self.parameters = (host_taps(up), host_taps(down), *_linear_params(alpha, beta))
         self.output = None
 
     def __call__(self, x):
@@ -169,4 +191,4 @@ def fir_quant(x, up, down, alpha, beta, smooth, scale):
     FP32 FIR math, then ``clamp(rint((y / smooth[c]) / scale))`` as int8."""
     a, ib = _linear_params(alpha, beta)
     s = float(scale) if not isinstance(scale, torch.Tensor) else float(scale.reshape(-1)[0])
-    return fir_snake(x, _filter(up), _filter(down), a, ib, smooth=smooth.float().contiguous(), scale=s)
+    return fir_snake(x, host_taps(up), host_taps(down), a, ib, smooth=smooth.float().contiguous(), scale=s)

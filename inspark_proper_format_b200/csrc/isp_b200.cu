@@ -209,16 +209,50 @@ int isp_fir_snake(const float* x, int64_t rows, int C, int64_t T, const float* u
   if (out_dtype != ISP_F32 && out_dtype != ISP_I8) return ISP_ERR_DTYPE;
   if (out_dtype == ISP_I8 && (smooth == nullptr || !(scale > 0.f))) return ISP_ERR_ARG;
   if (rows < 0 || C <= 0 || T <= 0 || (rows % C) != 0) return ISP_ERR_SHAPE;
+  if (T > (int64_t(1) << 40) || rows > 0x7FFFFFFFll) return ISP_ERR_SHAPE;
+  if (!isp::aligned16(x) || (out_dtype == ISP_F32 && (reinterpret_cast<uintptr_t>(y) & 7))) return ISP_ERR_ALIGN;
+  const bool bulk = T % 4 == 0;                         // rows fetched in 16-byte granules
   if (int st = isp::check_device()) return st;
   if (rows == 0) return ISP_OK;
   const int64_t tiles = (T + isp::kFirTile - 1) / isp::kFirTile;
-  const int64_t blocks = rows * tiles;
-  if (blocks > 0x7FFFFFFFll) return ISP_ERR_SHAPE;
-  isp::FirParams p{x, rows, C, T, tiles, up, down, alpha, inv_beta, y, smooth, scale};
-  if (out_dtype == ISP_F32)
-    isp::fir_snake_kernel<false><<<static_cast<unsigned>(blocks), isp::kFirThreads, 0, stream>>>(p);
-  else
-    isp::fir_snake_kernel<true><<<static_cast<unsigned>(blocks), isp::kFirThreads, 0, stream>>>(p);
+  isp::FirParams p{};
+  p.x = x;
+  p.rows = rows;
+  p.C = C;
+  p.T = T;
+  p.tiles_per_row = tiles;
+  p.alpha = alpha;
+  p.inv_beta = inv_beta;
+  p.y = y;
+  p.smooth = smooth;
+  p.scale = scale;
+  for (int k = 0; k < 12; ++k) {   // host arrays: the taps travel by value
+    p.up2[k] = 2.f * up[k];
+    p.down[k] = down[k];
+  }
+  auto kern = out_dtype == ISP_F32 ? (bulk ? isp::fir_snake_kernel<false, true> : isp::fir_snake_kernel<false, false>)
+                                   : (bulk ? isp::fir_snake_kernel<true, true> : isp::fir_snake_kernel<true, false>);
+  static bool configured[4][64] = {{false}};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int which = (out_dtype == ISP_F32 ? 0 : 2) + (bulk ? 1 : 0);
+  if (dev >= 0 && dev < 64 && !configured[which][dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, isp::kFirSmemBytes) != cudaSuccess)
+      return ISP_ERR_LAUNCH;
+    configured[which][dev] = true;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, isp::kFirThreads, isp::kFirSmemBytes) !=
+          cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int64_t total = rows * tiles;
+  const int64_t cap = static_cast<int64_t>(isp::sm_count()) * per_sm;
+  const unsigned grid = static_cast<unsigned>(total < cap ? total : cap);
+  p.g_rows = static_cast<int>(grid / tiles);
+  p.g_tiles = static_cast<int>(grid % tiles);
+  p.g_chan = p.g_rows % C;
+  kern<<<grid, isp::kFirThreads, isp::kFirSmemBytes, stream>>>(p);
   return isp::launch_status();
 }
 

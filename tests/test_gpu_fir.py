@@ -12,7 +12,9 @@ GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
 def rel_l2(a, b):
-    return float(np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(b), 1e-30))
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
 
 
 @pytest.fixture(scope="module")
@@ -28,7 +30,10 @@ def _params(c, seed):
 
 
 @pytest.mark.parametrize("b,c,t", [(1, 1, 1), (1, 3, 2), (2, 4, 5), (1, 2, 2047), (1, 2, 2048), (1, 2, 2049),
-                                   (2, 8, 4095), (1, 4, 6145), (3, 5, 301)])
+                                   (2, 8, 4095), (1, 4, 6145), (3, 5, 301),
+                                   # T % 4 == 0: streamed by bulk copies, incl. tiles that end past T
+                                   (1, 1, 4), (2, 3, 8), (1, 2, 12), (1, 3, 2052), (2, 2, 4100), (1, 3, 6144),
+                                   (3, 7, 16384)])
 def test_fir_matches_oracle(ops, b, c, t):
     f_up, f_down = ofir.bigvgan_filters()
     g = torch.Generator().manual_seed(t)
@@ -122,3 +127,20 @@ def test_full_size_row_properties(ops):
     yc = ops.fir_snake(const, torch.from_numpy(f_up).cuda(), torch.from_numpy(f_down).cuda(), alpha.cuda(), ib.cuda())
     expect = 0.3 + ib.numpy()[:, None] * np.sin(0.3 * alpha.numpy()[:, None]) ** 2
     np.testing.assert_allclose(yc[0].cpu().numpy(), np.broadcast_to(expect, (c, 4096)), rtol=2e-6, atol=2e-6)
+
+
+@pytest.mark.parametrize("alpha_scale,x_scale", [(60.0, 0.5), (1.0, 3e5), (1.0, 1e-30)])
+def test_fir_wide_snake_arguments(ops, alpha_scale, x_scale):
+    """Snake arguments from tiny to beyond the polynomial's reduction range
+    (|alpha v| > 1e6 takes CUDA's sinf): still within the FIR tolerance."""
+    f_up, f_down = ofir.bigvgan_filters()
+    c, t = 4, 3001
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(2, c, t, generator=g) * x_scale
+    alpha = (torch.rand(c, generator=g) * 1.5 + 0.5) * alpha_scale
+    ib = torch.from_numpy(ofir.snake_inverse_beta(alpha.numpy()))
+    y = ops.fir_snake(x.cuda(), torch.from_numpy(f_up).cuda(), torch.from_numpy(f_down).cuda(), alpha.cuda(),
+                      ib.cuda()).cpu().numpy()
+    ref = ofir.alias_free_snake(x.numpy(), f_up, f_down, alpha.numpy(), ib.numpy())
+    assert np.isfinite(y).all()
+    assert rel_l2(y, ref) < 2e-6
