@@ -278,6 +278,71 @@ def fir_component(torch, device, hbm_peak):
             "frac_hbm": round(gbs / hbm_peak, 3), "launches": 1}
 
 
+def run_case(args, torch, device, hbm_peak, bf16_peak):
+    """Single-kernel cases (profiling targets; inputs larger than L2):
+    gemm = the dominant cfg-2 projection, norm_quant = cfg-2 norm-quant,
+    fir = one cfg-5 micro-batch (B16 with --small)."""
+    from inspark_proper_format_b200 import _lib
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    g = torch.Generator(device=device).manual_seed(0)
+    if args.case == "gemm":
+        m, n, k = M_TOKENS, 1536, 512
+        a = (torch.randn(m, k, device=device, generator=g) * 50).clamp(-448, 448).to(torch.float8_e4m3fn)
+        w = (torch.randn(n, k, device=device, generator=g) * 50).clamp(-448, 448).to(torch.float8_e4m3fn)
+        ws = torch.rand(n, device=device, generator=g) * 1e-4
+        bias = torch.rand(n, device=device, generator=g)
+        out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+        fn = lib.isp_scaled_gemm
+        fargs = (a.data_ptr(), w.data_ptr(), _lib.E4M3, m, n, k, 0.01, None, ws.data_ptr(), bias.data_ptr(), None,
+                 _lib.F32, out.data_ptr(), _lib.BF16, 1.0, None, 0.0, stream)
+        nbytes, flops = gemm_bytes(m, n, k, "bf16"), 2 * m * n * k
+        name = f"gemm M={m} N={n} K={k} E4M3->BF16"
+    elif args.case == "norm_quant":
+        m, k = M_TOKENS, HIDDEN
+        x = torch.randn(m, k, device=device, generator=g).bfloat16()
+        gamma = torch.rand(k, device=device, generator=g) + 0.5
+        codes = torch.empty(m, k, device=device, dtype=torch.float8_e4m3fn)
+        fn = lib.isp_norm_quant
+        fargs = (x.data_ptr(), _lib.BF16, m, k, gamma.data_ptr(), None, 1e-6, 1.0, _lib.NORM_RMS_GPTFAST,
+                 _lib.Q_E4M3_STATIC, 0.02, None, codes.data_ptr(), None, stream)
+        nbytes, flops = m * k * 3, 0
+        name = f"norm_quant RMSNorm->E4M3 [{m},{k}] BF16"
+    else:
+        import ctypes
+
+        from inspark_proper_format_b200.alias_free import host_taps, kaiser_sinc_filter, snake_inverse_beta
+        b, c, t = (16 if args.small else 64), 512, 16384
+        x = torch.randn(b, c, t, device=device, generator=g) * 0.5
+        y = torch.empty_like(x)
+        taps = host_taps(kaiser_sinc_filter())
+        alpha = torch.rand(c, device=device, generator=g) * 1.5 + 0.5
+        ib = snake_inverse_beta(alpha).contiguous()
+        fn = lib.isp_fir_snake
+        fargs = (x.data_ptr(), b * c, c, t, ctypes.addressof(taps), ctypes.addressof(taps), alpha.data_ptr(),
+                 ib.data_ptr(), y.data_ptr(), _lib.F32, None, 0.0, stream)
+        nbytes, flops = 8 * b * c * t, 0
+        name = f"fir B{b}xC{c}xT{t} FP32"
+    for _ in range(args.warmup):
+        _lib.check(fn(*fargs), args.case)
+    torch.cuda.synchronize(device)
+    times = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn(*fargs)
+        e1.record()
+        torch.cuda.synchronize(device)
+        times.append(e0.elapsed_time(e1) / 1e3)
+    sec = statistics.median(times)
+    line = {"case": args.case, "kernel": name, "us": round(sec * 1e6, 2), "GB/s": round(nbytes / sec / 1e9, 1),
+            "frac_hbm": round(nbytes / sec / 1e9 / hbm_peak, 3), "launches": args.steps + args.warmup}
+    if flops:
+        line["TFLOP/s"] = round(flops / sec / 1e12, 1)
+        line["frac_fp8"] = round(flops / sec / 1e12 / (2 * bf16_peak), 3)
+    print(json.dumps(line), flush=True)
+
+
 def cpu_sample_layer(m_rows, seed=0):
     """One cfg-2 layer of the reference's torch CPU path on m_rows tokens."""
     import torch
@@ -356,6 +421,9 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-components", action="store_true")
+    ap.add_argument("--case", choices=("stack", "gemm", "norm_quant", "fir"), default="stack",
+                    help="stack = the headline step; the others time one kernel (profiling targets)")
+    ap.add_argument("--small", action="store_true", help="smaller FIR case for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -380,6 +448,12 @@ def main():
 
     hbm_peak, bf16_peak, peak_kind = peaks()
     fp8_peak = 2.0 * bf16_peak
+    if args.case != "stack":
+        if rank == 0:
+            run_case(args, torch, device, hbm_peak, bf16_peak)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     stack = Stack(device, seed=1234 + rank)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)   # > 126 MB L2
 
@@ -429,6 +503,11 @@ def main():
         roof = {"bound": "tensor", "achieved": round(dom_flops / dom_s / 1e12, 1), "peak": fp8_peak, "unit": "TFLOP/s"}
     roof["frac"] = round(roof["achieved"] / roof["peak"], 3)
     roof["traffic"] = None
+    try:   # DRAM read+write per launch from the committed ncu capture of this kernel
+        with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
+            roof["traffic"] = json.load(f)["gemm_attn_in"]["dram_bytes_per_launch"]
+    except (OSError, KeyError, ValueError):
+        pass
     roof["kernel"] = f"gemm {DOMINANT} (M={stack.m}, N=1536, K=512, E4M3 in, BF16 out), {len(dom)} launches"
     roof["us_per_launch"] = round(dom_s * 1e6, 2)
     roof["peak_source"] = peak_kind + (" (fp8 tensor peak = 2 x measured bf16)" if roof["bound"] == "tensor" else "")
