@@ -435,24 +435,19 @@ def main():
         return
 
     import torch
-    import torch.distributed as dist
+
+    from inspark_proper_format_b200.dp import RankContext, weak_scaling_throughput
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    ctx = RankContext(rank, world, local_rank, "nccl").init(timeout_s=300.0, device=device)
+    barrier = ctx.barrier
 
     hbm_peak, bf16_peak, peak_kind = peaks()
     fp8_peak = 2.0 * bf16_peak
     if args.case != "stack":
         if rank == 0:
             run_case(args, torch, device, hbm_peak, bf16_peak)
-        if world > 1:
-            dist.destroy_process_group()
+        ctx.close()
         return
     stack = Stack(device, seed=1234 + rank)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)   # > 126 MB L2
@@ -483,13 +478,9 @@ def main():
         torch.cuda.synchronize(device)
     barrier()
     step_s = [a.elapsed_time(b) / 1e3 for a, b in step_events]
-    total = sum(step_s)
-    if world > 1:
-        t = torch.tensor([total], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total = float(t.item())
+    total = ctx.max_over_ranks(sum(step_s), device=device)      # the job ends with the slowest rank
     ms_per_step = total / args.steps * 1e3
-    value = world * stack.flops() * args.steps / total / 1e12
+    value = weak_scaling_throughput(stack.flops() * args.steps, world, total) / 1e12
 
     # dominant kernel roofline (attn_in: 512 -> 1536, BF16 out)
     dom = [a.elapsed_time(b) / 1e3 for a, b in ev[DOMINANT][2]]
@@ -531,12 +522,8 @@ def main():
         e1.record()
         torch.cuda.synchronize(device)
         e2e_s.append(e0.elapsed_time(e1) / 1e3)
-    e2e_total = sum(e2e_s)
-    if world > 1:
-        t = torch.tensor([e2e_total], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_total = float(t.item())
-    e2e_value = world * stack.flops() * len(e2e_s) / e2e_total / 1e12
+    e2e_total = ctx.max_over_ranks(sum(e2e_s), device=device)
+    e2e_value = weak_scaling_throughput(stack.flops() * len(e2e_s), world, e2e_total) / 1e12
 
     components = {
         "gemm_all": {"TFLOP/s": round(value / world, 1), "frac_fp8_peak": round(value / world / fp8_peak, 3)},
@@ -567,9 +554,8 @@ def main():
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        barrier()
-        dist.destroy_process_group()
+    barrier()
+    ctx.close()
 
 
 if __name__ == "__main__":
