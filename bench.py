@@ -308,6 +308,36 @@ def run_case(args, torch, device, hbm_peak, bf16_peak):
                  _lib.Q_E4M3_STATIC, 0.02, None, codes.data_ptr(), None, stream)
         nbytes, flops = m * k * 3, 0
         name = f"norm_quant RMSNorm->E4M3 [{m},{k}] BF16"
+    elif args.case in ("nvfp4_gated_up", "nvfp4_down"):
+        # config 3: gated-up M=51200, K=512, N=2x2048 (NVFP4 h out), down 2048 -> 512 (BF16 out)
+        m = 51200
+        n, k = (2048, 512) if args.case == "nvfp4_gated_up" else (512, 2048)
+        rows_w = 2 * n if args.case == "nvfp4_gated_up" else n
+
+        def sf_bytes(r, kk):
+            return (r + 127) // 128 * 128 * kk // 16
+
+        a = torch.randint(0, 256, (m, k // 2), device=device, generator=g, dtype=torch.uint8)
+        a_sf = torch.randint(0x28, 0x40, (sf_bytes(m, k),), device=device, generator=g, dtype=torch.uint8)
+        w = torch.randint(0, 256, (rows_w, k // 2), device=device, generator=g, dtype=torch.uint8)
+        w_sf = torch.randint(0x28, 0x40, (sf_bytes(rows_w, k),), device=device, generator=g, dtype=torch.uint8)
+        if args.case == "nvfp4_gated_up":
+            h = torch.empty(m, n // 2, device=device, dtype=torch.uint8)
+            h_sf = torch.empty(sf_bytes(m, n), device=device, dtype=torch.uint8)
+            fn = lib.isp_nvfp4_gated_up
+            fargs = (a.data_ptr(), a_sf.data_ptr(), w.data_ptr(), w_sf.data_ptr(), m, n, k, 1e-3, 1e-3, 0.01,
+                     h.data_ptr(), h_sf.data_ptr(), stream)
+            nbytes = m * k // 2 + sf_bytes(m, k) + rows_w * k // 2 + m * n // 2 + sf_bytes(m, n)
+            flops = 2 * m * rows_w * k
+            name = f"nvfp4 gated-up M={m} N=2x{n} K={k} -> NVFP4 h"
+        else:
+            out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+            fn = lib.isp_nvfp4_gemm
+            fargs = (a.data_ptr(), a_sf.data_ptr(), w.data_ptr(), w_sf.data_ptr(), m, n, k, 1e-3, None, None,
+                     _lib.F32, out.data_ptr(), _lib.BF16, stream)
+            nbytes = m * k // 2 + sf_bytes(m, k) + rows_w * k // 2 + m * n * 2
+            flops = 2 * m * n * k
+            name = f"nvfp4 gemm M={m} N={n} K={k} -> BF16"
     else:
         import ctypes
 
@@ -339,7 +369,8 @@ def run_case(args, torch, device, hbm_peak, bf16_peak):
             "frac_hbm": round(nbytes / sec / 1e9 / hbm_peak, 3), "launches": args.steps + args.warmup}
     if flops:
         line["TFLOP/s"] = round(flops / sec / 1e12, 1)
-        line["frac_fp8"] = round(flops / sec / 1e12 / (2 * bf16_peak), 3)
+        fp4 = args.case.startswith("nvfp4")
+        line["frac_fp4" if fp4 else "frac_fp8"] = round(flops / sec / 1e12 / ((4 if fp4 else 2) * bf16_peak), 3)
     print(json.dumps(line), flush=True)
 
 
@@ -421,7 +452,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-components", action="store_true")
-    ap.add_argument("--case", choices=("stack", "gemm", "norm_quant", "fir"), default="stack",
+    ap.add_argument("--case", choices=("stack", "gemm", "norm_quant", "fir", "nvfp4_gated_up", "nvfp4_down"),
+                    default="stack",
                     help="stack = the headline step; the others time one kernel (profiling targets)")
     ap.add_argument("--small", action="store_true", help="smaller FIR case for ncu captures")
     args = ap.parse_args()

@@ -63,7 +63,12 @@ enum isp_qfmt {
   /* NVFP4: 16-element blocks, E4M3 block scale e4m3(amax_b / (6 g)), E2M1
      codes of y / (s_b g) packed low nibble = even k;
      scripts/export_nvfp4_weights.py:25-42 */
-  ISP_Q_NVFP4 = 3
+  ISP_Q_NVFP4 = 3,
+  /* NVFP4 as above, block scales written in the tensor-core layout consumed by
+     isp_nvfp4_gemm: 128-row x 4-block chunks of 512 bytes, byte
+     ((m/128)*(K/64) + k16/4)*512 + (m%32)*16 + ((m%128)/32)*4 + k16%4
+     (scales_out holds ceil(M/128)*128*K/16 bytes; K % 64 == 0). */
+  ISP_Q_NVFP4_MMA = 4
 };
 
 int isp_version(void);
@@ -93,15 +98,27 @@ int isp_read_device_error(int *error_out, int clear, isp_stream_t stream);
  * gamma:  [K] FP32 (RMS kinds), bias: [K] FP32 (ISP_NORM_BIAS), else NULL.
  * out_mul: exp(log_scale) for ISP_NORM_BIAS (ignored otherwise).
  * scale:  ISP_Q_E4M3_STATIC / ISP_Q_INT8_STATIC: the per-tensor scale;
- *         ISP_Q_NVFP4: the FP32 global scale g; ignored for ISP_Q_E4M3_ROW.
+ *         NVFP4 formats: the FP32 global scale g; ignored for ISP_Q_E4M3_ROW.
+ *         Must lie in [2^-100, 2^100] (quotients are then exactly rounded).
  * smooth: [K] FP32 SmoothQuant divisor (ISP_Q_INT8_STATIC) or NULL.
  * codes:  [M, K] uint8/int8 codes, or [M, K/2] packed E2M1 for NVFP4.
- * scales_out: FP32 [M] (ISP_Q_E4M3_ROW), E4M3 [M, K/16] (ISP_Q_NVFP4), else NULL.
+ * scales_out: FP32 [M] (ISP_Q_E4M3_ROW), E4M3 [M, K/16] (ISP_Q_NVFP4), the
+ *   tensor-core layout (ISP_Q_NVFP4_MMA: ceil(M/128)*128*K/16 bytes, K % 64
+ *   == 0; bytes of rows >= M are not written and do not affect rows < M of an
+ *   isp_nvfp4_gemm), else NULL.
  */
 int isp_norm_quant(const void *x, int x_dtype, int64_t M, int K,
                    const float *gamma, const float *bias, float eps, float out_mul,
                    int norm_kind, int qfmt, float scale, const float *smooth,
                    void *codes, void *scales_out, isp_stream_t stream);
+
+/*
+ * Reorders E4M3 block scales [R, K/16] (row-major, the ModelOpt storage order
+ * of scripts/export_nvfp4_weights.py:38) into the tensor-core layout described
+ * at ISP_Q_NVFP4_MMA.  dst must hold ceil(R/128)*128*K/16 bytes; padding rows
+ * are written as zero.  K % 64 == 0.
+ */
+int isp_nvfp4_scales_to_mma(const void *src, int64_t R, int K, void *dst, isp_stream_t stream);
 
 /*
  * BigVGAN anti-aliased Snake activation: 2x 12-tap polyphase upsample with
@@ -169,6 +186,54 @@ int isp_scaled_gemm(const void *A, const void *W, int ab_dtype, int64_t M, int N
 int isp_gated_up(const void *A, const void *W1, const void *W3, int interleaved,
                  int64_t M, int N, int K, const float *s1, const float *s3,
                  float out_scale, void *out, int out_dtype, isp_stream_t stream);
+
+/*
+ * NVFP4 block-scaled GEMM on tcgen05 tensor cores (kind::mxf4nvf4, 16-element
+ * K blocks, E4M3 block scales):
+ *   v[m, n] = alpha * sum_k (e2m1(A[m,k]) sa[m,k/16]) (e2m1(W[n,k]) sw[n,k/16])
+ *             + bias[n] + residual[m, n]
+ * with alpha = activation global scale * weight global scale.
+ *
+ * Replaces: MatrixWeightOp.forward with the ModelOpt NVFP4 quantizers applied
+ *   (build/nvfp4_graph.py:73-87, installed by quantization/nvfp4.py:11-56),
+ *   i.e. TensorRT's native FP4 GEMM behind NVFP4 Q/DQ.
+ *
+ * A: [M, K/2] packed E2M1 (low nibble = even k); A_sf: A's block scales in
+ *   the tensor-core layout (ISP_Q_NVFP4_MMA, as written by isp_norm_quant).
+ * W: [N, K/2] packed E2M1; W_sf: the weight's scales in the same layout
+ *   (isp_nvfp4_scales_to_mma of the exporter's [N, K/16] block_scale).
+ * K % 64 == 0, N % 8 == 0; A, W, A_sf, W_sf, out 16-byte aligned.
+ * out: [M, N] in out_dtype (ISP_BF16, ISP_F16 or ISP_F32).  bias: [N] FP32 or
+ *   NULL; residual: [M, N] ISP_F32 / ISP_BF16 or NULL.
+ */
+int isp_nvfp4_gemm(const void *A, const void *A_sf, const void *W, const void *W_sf,
+                   int64_t M, int N, int K, float alpha, const float *bias,
+                   const void *residual, int residual_dtype, void *out, int out_dtype,
+                   isp_stream_t stream);
+
+/*
+ * NVFP4 CFM gated-up: gate = alpha_gate * (A . W1^T), up = alpha_up * (A . W3^T),
+ * h = silu(gate) * up, requantized to NVFP4 with the FP32 global scale h_scale
+ * (the down projection's calibrated activation global scale):
+ *   s_b = e4m3(min(amax_b / (6 h_scale), 448)) (an all-zero block: 1),
+ *   code = e2m1(h / (s_b h_scale)).
+ *
+ * Replaces: FeedForward.forward w1/w3/silu (gpt_fast/model.py:235-244) under the
+ *   NVFP4 recipe (quantization/nvfp4.py:58-68): two native FP4 GEMMs, the
+ *   SiLU-gate, and the dynamic block quantization of the w2 input.
+ *
+ * A, A_sf: as isp_nvfp4_gemm (K % 64 == 0).
+ * W13: [2N, K/2] packed E2M1, gate and up rows stacked in blocks of 64:
+ *   rows [128 j, 128 j + 64) = W1 rows [64 j, 64 j + 64), rows
+ *   [128 j + 64, 128 j + 128) = W3 rows [64 j, 64 j + 64); W13_sf: its scales in
+ *   the tensor-core layout.  N % 64 == 0.
+ * h_codes: [M, N/2] packed E2M1; h_sf: ceil(M/128)*128*N/16 bytes, the
+ *   tensor-core layout of an [M, N] operand (feeds isp_nvfp4_gemm directly).
+ * h_scale must lie in [2^-100, 2^100].
+ */
+int isp_nvfp4_gated_up(const void *A, const void *A_sf, const void *W13, const void *W13_sf,
+                       int64_t M, int N, int K, float alpha_gate, float alpha_up, float h_scale,
+                       void *h_codes, void *h_sf, isp_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -16,7 +16,7 @@ LIB_PATH = PACKAGE_DIR / "libisp_b200.so"
 ISP_OK, ISP_ERR_SHAPE, ISP_ERR_ALIGN, ISP_ERR_DTYPE, ISP_ERR_ARCH, ISP_ERR_LAUNCH, ISP_ERR_TIMEOUT, ISP_ERR_ARG = range(8)
 BF16, F32, F16, E4M3, I8, E2M1, I32 = range(7)
 NORM_NONE, NORM_RMS_GPTFAST, NORM_RMS_QWEN, NORM_BIAS = range(4)
-Q_E4M3_STATIC, Q_E4M3_ROW, Q_INT8_STATIC, Q_NVFP4 = range(4)
+Q_E4M3_STATIC, Q_E4M3_ROW, Q_INT8_STATIC, Q_NVFP4, Q_NVFP4_MMA = range(5)
 
 _vp, _i, _i64, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 
@@ -30,6 +30,9 @@ SIGNATURES = {
     "isp_fir_snake": (_i, [_vp, _i64, _i, _i64, _vp, _vp, _vp, _vp, _vp, _i, _vp, _f, _vp]),
     "isp_scaled_gemm": (_i, [_vp, _vp, _i, _i64, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _vp, _i, _f, _vp, _f, _vp]),
     "isp_gated_up": (_i, [_vp, _vp, _vp, _i, _i64, _i, _i, _vp, _vp, _f, _vp, _i, _vp]),
+    "isp_nvfp4_scales_to_mma": (_i, [_vp, _i64, _i, _vp, _vp]),
+    "isp_nvfp4_gemm": (_i, [_vp, _vp, _vp, _vp, _i64, _i, _i, _f, _vp, _vp, _i, _vp, _i, _vp]),
+    "isp_nvfp4_gated_up": (_i, [_vp, _vp, _vp, _vp, _i64, _i, _i, _f, _f, _f, _vp, _vp, _vp]),
 }
 
 _LIB = None

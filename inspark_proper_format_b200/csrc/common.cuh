@@ -33,7 +33,7 @@ __device__ int g_device_error = 0;
 
 // ---------------------------------------------------------------------------
 // Number formats (device).  E4M3 conversion uses the hardware cvt with
-// round-to-nearest-even; callers clamp to +-448 first, as the reference does.
+// round-to-nearest-even and saturation to +-448 (NaN stays NaN).
 // ---------------------------------------------------------------------------
 // Packs two floats into two E4M3 bytes: `lo` goes to bits 0-7, `hi` to 8-15.
 ISP_D uint16_t e4m3x2(float lo, float hi) {
@@ -60,6 +60,24 @@ ISP_D uint32_t e2m1_code(float v) {
   uint32_t m = (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) +
                (a >= 3.5f) + (a > 5.0f);
   return m | (v < 0.f ? 8u : 0u);
+}
+
+// RN(x / d) from a reciprocal y = RN(1/d) shared by many quotients (one
+// reciprocal per scale instead of one division per element).  Markstein's
+// correction (P. Markstein, IBM J. Res. Dev. 34(1), 1990; Muller et al.,
+// "Handbook of Floating-Point Arithmetic", ch. 4): q = RN(x y), the residual
+// r = x - q d is exact in one FMA, and RN(q + r y) is the correctly rounded
+// quotient.  The correction is applied twice.  Exact for normal d below
+// 2^126; when the first product is out of range (|q| >= 2^100, inf, NaN) or
+// d is zero or at least 2^126, x * y is returned, which equals x / d up to the
+// saturation every caller applies next (inf, NaN and 0 propagate as in x / d).
+ISP_D float div_rn_recip(float x, float d, float y) {
+  const float q0 = __fmul_rn(x, y);
+  float r = __fmaf_rn(-q0, d, x);
+  float q = __fmaf_rn(r, y, q0);
+  r = __fmaf_rn(-q, d, x);
+  q = __fmaf_rn(r, y, q);
+  return (fabsf(q0) < 0x1p100f && fabsf(d) < 0x1p126f) ? q : q0;
 }
 
 ISP_D int8_t int8_rne_sat(float v) {

@@ -1,6 +1,10 @@
-// W8A8 (E4M3 / INT8) GEMM on 5th-generation tensor cores (tcgen05), sm_100a.
+// W8A8 (E4M3 / INT8) and NVFP4 GEMM on 5th-generation tensor cores (tcgen05),
+// sm_100a.
 //
-// out[M, N] = epilogue(A[M, K] . B[N, K]^T), both operands K-major 8-bit.
+// out[M, N] = epilogue(A[M, K] . B[N, K]^T), both operands K-major: 8-bit codes
+// (kind::f8f6f4 / kind::i8), or packed E2M1 with one E4M3 scale per 16 K
+// (kind::mxf4nvf4.block_scale.block16).  A stage always holds 128 bytes of K
+// per row (128 8-bit or 256 4-bit elements).
 //
 // Persistent, warp-specialized CTA (192 threads, one CTA per SM):
 //   warp 0      TMA producer: A and B tiles (BK = 128 bytes of K, 128-byte
@@ -9,9 +13,14 @@
 //               tcgen05.mma (M = 128, N = BN, K = 32 per instruction) into one
 //               of two TMEM accumulators, so the epilogue of tile i overlaps
 //               the main loop of tile i+1.
-//   warps 2..5  epilogue: tcgen05.ld (32 lanes x 32 columns per load), fused
+//   warps 2..   epilogue: tcgen05.ld (32 lanes x 32 columns per load), fused
 //               scale / bias / residual / SwiGLU / requant, 128-byte swizzled
-//               staging and TMA stores.
+//               staging and TMA stores (NVFP4 outputs: direct 16-byte stores).
+// NVFP4 adds the block scales: each stage carries 2 KB of A scales and 2 KB of
+// B scales (four 512-byte chunks of 128 rows x 4 scales each, copied in the
+// tensor-core layout by one bulk copy per operand), which the MMA thread moves
+// into TMEM with tcgen05.cp (32 lanes x 128 bits, replicated to the 4 lane
+// quarters) right before the four K = 64 MMAs that read them.
 // Every mbarrier wait is bounded (~1 s); on expiry the waiting thread records
 // ISP_ERR_TIMEOUT in g_device_error, raises the CTA abort flag, and all roles
 // unwind to the common exit, which drains in-flight TMA/MMA work and frees TMEM.
@@ -40,10 +49,16 @@ struct Roles {
   static constexpr int kHalves = kEpiWarps / 4;
 };
 
+enum AbKind { AB_E4M3 = 0, AB_I8 = 1, AB_FP4 = 2 };
 enum EpiKind { EPI_SCALE = 0, EPI_SWIGLU_PAIRED = 1, EPI_SWIGLU_INTERLEAVED = 2 };
-enum OutKind { OUT_BF16 = 0, OUT_F16 = 1, OUT_F32 = 2, OUT_E4M3 = 3 };
+// OUT_NVFP4: packed E2M1 codes + E4M3 block scales in the tensor-core layout.
+enum OutKind { OUT_BF16 = 0, OUT_F16 = 1, OUT_F32 = 2, OUT_E4M3 = 3, OUT_NVFP4 = 4 };
 
-ISP_HD int out_bytes(int out) { return out == OUT_F32 ? 4 : (out == OUT_E4M3 ? 1 : 2); }
+ISP_HD int out_bytes(int out) { return out == OUT_F32 ? 4 : ((out == OUT_E4M3 || out == OUT_NVFP4) ? 1 : 2); }
+
+constexpr int kSfChunk = 512;                        // 128 rows x 4 E4M3 scales (K = 64)
+constexpr int kSfOperandBytes = 4 * kSfChunk;        // one operand's scales for a 256-element K stage
+constexpr int kSfStageBytes = 2 * kSfOperandBytes;   // A and B scales of one stage
 
 struct Params {
   int M, N, K;            // N = logical output columns
@@ -59,13 +74,24 @@ struct Params {
   float out_scale;        // SwiGLU dequant multiplier (F32 output)
   void* out2;             // residual-dual E4M3 output
   float out2_inv;
+  // NVFP4 operands: block scales of A and B in the tensor-core layout
+  // (chunk (r/128, k/64) of 512 bytes at ((r/128) * k_chunks + k/64) * 512).
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  int k_chunks;           // K / 64
+  float alpha_up;         // NVFP4 SwiGLU: up-projection dequant (gate: a_scale)
+  float q_scale;          // NVFP4 output: global scale of h
+  uint8_t* q_codes;       // NVFP4 output: packed E2M1 [M, N/2]
+  uint8_t* q_sf;          // NVFP4 output: block scales, tensor-core layout
 };
 
-template <int kBN, int kStages, int kEpiWarps>
+template <int kBN, int kStages, int kEpiWarps, int kSfBytes = 0>
 struct Smem {
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = kBN * kBK;
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfBytes;   // [A | B | A scales | B scales]
+  static constexpr int ab(int s) { return s * kStageBytes; }
+  static constexpr int sf(int s) { return s * kStageBytes + kABytes + kBBytes; }
   static constexpr int kStagingBytes = kEpiWarps * kStagingBufs * 32 * 128;  // per warp: buffers of 32 rows x 128 B
   static constexpr int kParamOffset = kStages * kStageBytes + kStagingBytes;
   static constexpr int kParamBytes = 512 * 4;              // per-tile column scales / bias
@@ -129,6 +155,13 @@ ISP_D void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0, in
                "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
                : "memory");
 }
+// 1-D bulk copy global -> shared, completing on an mbarrier (16-byte aligned, size % 16 == 0).
+ISP_D void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 ISP_D void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 ISP_D void bulk_wait_read_le1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 ISP_D void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -152,12 +185,46 @@ ISP_D uint64_t smem_desc_sw128(uint32_t addr) {
   return d;
 }
 
-template <bool kInt8, int kBN>
+// Scale-factor chunk in shared memory: 32 rows x 16 bytes, no swizzle; the
+// 8-row core matrices are 128 bytes apart (stride byte offset).
+ISP_D uint64_t smem_desc_sf(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;                  // leading byte offset (one core matrix along K)
+  d |= static_cast<uint64_t>(128 >> 4) << 32;           // stride byte offset
+  d |= static_cast<uint64_t>(1) << 46;                  // descriptor version (sm_100); layout 0 = no swizzle
+  return d;
+}
+
+template <int kAB, int kBN>
 ISP_HD uint32_t instr_desc() {
-  // D format (F32 = 1, S32 = 2), A/B format (E4M3 = 0, signed int8 = 1), K-major A and B,
-  // N >> 3 at bit 17, M >> 4 at bit 24.
-  return (kInt8 ? (2u << 4) : (1u << 4)) | (kInt8 ? (1u << 7) | (1u << 10) : 0u) |
-         (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+  if constexpr (kAB == AB_FP4) {
+    // Block-scaled descriptor: A/B format E2M1 (1) at bits 7 and 10, scale
+    // format UE4M3 (0) at bit 23, scale-factor ids 0, N >> 3 at 17, M >> 4 at 24.
+    return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+           (static_cast<uint32_t>(kBM >> 4) << 24);
+  } else {
+    // D format (F32 = 1, S32 = 2), A/B format (E4M3 = 0, signed int8 = 1), K-major A and B,
+    // N >> 3 at bit 17, M >> 4 at bit 24.
+    constexpr bool kInt8 = kAB == AB_I8;
+    return (kInt8 ? (2u << 4) : (1u << 4)) | (kInt8 ? (1u << 7) | (1u << 10) : 0u) |
+           (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+  }
+}
+
+// SMEM -> TMEM copy of one scale chunk: 32 lanes x 128 bits, replicated into
+// all four 32-lane quarters (4 TMEM columns).
+ISP_D void tmem_cp_sf(uint32_t taddr, uint64_t src_desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc) : "memory");
+}
+
+ISP_D void mma_fp4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t sfa_tmem,
+                   uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem));
 }
 
 template <bool kInt8>
@@ -431,15 +498,58 @@ ISP_D void swiglu_group(const uint32_t (&a)[32], const uint32_t (&b)[32], const 
   }
 }
 
+// NVFP4 SwiGLU of one 32-output group of one row:
+//   h = silu(acc_gate * alpha_gate) * (acc_up * alpha_up)
+// quantized as two 16-element blocks with the global scale gq:
+//   s = e4m3(min(amax / (6 gq), 448)) (an all-zero block takes s = 1),
+//   code = e2m1(h / (s gq)), low nibble = even column.
+// The codes go to `codes` (16 bytes); the two scale bytes are returned.
+ISP_D uint32_t swiglu_nvfp4_group(const uint32_t (&a)[32], const uint32_t (&b)[32], float ag, float au, float gq,
+                                  float six_gq, uint4& codes) {
+  float h[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    h[j] = silu_mul(__fmul_rn(__uint_as_float(a[j]), ag), __fmul_rn(__uint_as_float(b[j]), au));
+  uint32_t w[4];
+  uint32_t sf = 0;
+#pragma unroll
+  for (int blk = 0; blk < 2; ++blk) {
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(h[16 * blk + j]));
+    float sb = __fdiv_rn(amax, six_gq);
+    if (sb == 0.f) sb = 1.f;
+    const uint32_t sc = e4m3x2(fminf(sb, 448.f), 0.f) & 0xFFu;
+    const float denom = __fmul_rn(e4m3_to_f32(static_cast<uint8_t>(sc)), gq);
+    const float rden = __frcp_rn(denom);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t packed = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        packed |= e2m1_code(div_rn_recip(h[16 * blk + 8 * half + j], denom, rden)) << (4 * j);
+      w[2 * blk + half] = packed;
+    }
+    sf |= sc << (8 * blk);
+  }
+  codes = make_uint4(w[0], w[1], w[2], w[3]);
+  return sf;
+}
+
 // ----------------------------------------------------------------------------
 // The kernel
 // ----------------------------------------------------------------------------
-template <int kBN, int kStages, int kEpiWarps, bool kInt8, int kEpi, int kOut>
+template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut>
 __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_out,
                 const Params p) {
-  using L = Smem<kBN, kStages, kEpiWarps>;
+  constexpr bool kInt8 = kAB == AB_I8;
+  constexpr bool kFp4 = kAB == AB_FP4;
+  static_assert(!kFp4 || kBN == 128, "NVFP4 tiles are 128 x 128 (one scale chunk per operand and K = 64)");
+  static_assert(kOut != OUT_NVFP4 || (kFp4 && kEpi == EPI_SWIGLU_PAIRED), "NVFP4 output is the FP4 SwiGLU epilogue");
+  using L = Smem<kBN, kStages, kEpiWarps, kFp4 ? kSfStageBytes : 0>;
+  static_assert(L::kStageBytes % 1024 == 0, "every stage's swizzled A/B tiles start 1024-byte aligned");
   using R = Roles<kEpiWarps>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // The 128-byte swizzle patterns assume a 1024-byte aligned base; refuse to run otherwise.
@@ -460,7 +570,9 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr int kTmemCols = 2 * kBN;             // two accumulators (power of two, >= 32)
+  // Two accumulators (power of two, >= 32); NVFP4 adds 32 scale columns per stage after them.
+  constexpr int kTmemCols = kFp4 ? 512 : 2 * kBN;
+  static_assert(!kFp4 || 2 * kBN + 32 * kStages <= 512, "TMEM columns");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -477,7 +589,7 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     prefetch_tmap(&tm_a);
     prefetch_tmap(&tm_b);
     if constexpr (kEpi == EPI_SWIGLU_PAIRED) prefetch_tmap(&tm_b2);
-    prefetch_tmap(&tm_out);
+    if constexpr (kOut != OUT_NVFP4) prefetch_tmap(&tm_out);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -506,13 +618,24 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         const int nt = tile % p.n_tiles;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
-          uint8_t* sa = smem + stage * L::kStageBytes;
+          uint8_t* sa = smem + L::ab(stage);
           uint8_t* sb = sa + L::kABytes;
-          mbar_expect_tx(&full_bar[stage], L::kStageBytes);
+          if constexpr (kFp4) {
+            // scale chunks of this stage (K = 256 -> up to four 512-byte chunks per operand)
+            const int nch = min(4, p.k_chunks - 4 * kb);
+            const uint32_t sf_bytes = static_cast<uint32_t>(nch) * kSfChunk;
+            mbar_expect_tx(&full_bar[stage], L::kABytes + L::kBBytes + 2 * sf_bytes);
+            const int64_t a_off = (static_cast<int64_t>(m0 / kBM) * p.k_chunks + 4 * kb) * kSfChunk;
+            const int64_t b_off = (static_cast<int64_t>(nt) * p.k_chunks + 4 * kb) * kSfChunk;
+            bulk_load(smem + L::sf(stage), p.sfa + a_off, sf_bytes, &full_bar[stage]);
+            bulk_load(smem + L::sf(stage) + kSfOperandBytes, p.sfb + b_off, sf_bytes, &full_bar[stage]);
+          } else {
+            mbar_expect_tx(&full_bar[stage], L::kStageBytes);
+          }
           armed[stage] = true;
           armed_phase[stage] = phase;
           tma_load_2d(sa, &tm_a, &full_bar[stage], kb * kBK, m0);
-          if constexpr (kEpi == EPI_SWIGLU_PAIRED) {
+          if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
             tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * (kBN / 2));
             tma_load_2d(sb + (kBN / 2) * kBK, &tm_b2, &full_bar[stage], kb * kBK, nt * (kBN / 2));
           } else {
@@ -528,7 +651,7 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = instr_desc<kInt8, kBN>();
+      const uint32_t idesc = instr_desc<kAB, kBN>();
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -542,12 +665,29 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!wait_bounded(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t a_addr = smem_u32(smem + L::ab(stage));
           const uint32_t b_addr = a_addr + L::kABytes;
+          if constexpr (kFp4) {
+            // Scales -> TMEM (A at columns +0..15, B at +16..31 of this stage's slot),
+            // then one K = 64 MMA per chunk; tcgen05.cp and tcgen05.mma issued by one
+            // thread execute in order.
+            const int nch = min(4, p.k_chunks - 4 * kb);
+            const uint32_t sf_t = tmem_base + static_cast<uint32_t>(2 * kBN + 32 * stage);
+            const uint32_t sf_s = smem_u32(smem + L::sf(stage));
+            for (int c = 0; c < nch; ++c) {
+              tmem_cp_sf(sf_t + 4 * c, smem_desc_sf(sf_s + c * kSfChunk));
+              tmem_cp_sf(sf_t + 16 + 4 * c, smem_desc_sf(sf_s + kSfOperandBytes + c * kSfChunk));
+            }
+            for (int kk = 0; kk < nch; ++kk) {
+              mma_fp4(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
+                      sf_t + 4 * kk, sf_t + 16 + 4 * kk, (kb | kk) != 0);
+            }
+          } else {
 #pragma unroll
-          for (int kk = 0; kk < kBK / 32; ++kk) {
-            mma_issue<kInt8>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
-                             (kb | kk) != 0);
+            for (int kk = 0; kk < kBK / 32; ++kk) {
+              mma_issue<kInt8>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
+                               (kb | kk) != 0);
+            }
           }
           issued = true;
           mma_commit(&empty_bar[stage]);
@@ -578,21 +718,24 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     constexpr int kChunkCols = 128 / (kOut == OUT_F32 ? 4 : (kOut == OUT_E4M3 ? 1 : 2));
     constexpr int kGroupsPerChunk = kChunkCols / 32;
     constexpr int kGroups = kOutCols / 32 / R::kHalves;   // 32-column groups this warp handles
-    static_assert(kGroups % kGroupsPerChunk == 0, "a warp's columns must be whole store boxes");
+    static_assert(kOut == OUT_NVFP4 || kGroups % kGroupsPerChunk == 0, "a warp's columns must be whole store boxes");
+    constexpr bool kParams = !(kFp4 && kEpi != EPI_SCALE);   // NVFP4 SwiGLU takes scalar dequant factors
     const int g0 = half * kGroups;
     constexpr int kWordsPerGroup = 32 / kGroupsPerChunk;
     TileParams<kEpi, kBN, R::kEpiThreads> tp;
-    if (blockIdx.x < total_tiles) tp.fetch(p, (blockIdx.x % p.n_tiles) * kOutCols, et);
+    if (kParams && blockIdx.x < total_tiles) tp.fetch(p, (blockIdx.x % p.n_tiles) * kOutCols, et);
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
       const int m0 = (tile / p.n_tiles) * kBM;
       const int n0 = (tile % p.n_tiles) * kOutCols;
       // Per-column parameters of this tile -> shared memory (zero past column N),
       // then start fetching the next tile's.
-      epilogue_sync<R::kEpiThreads>();
-      tp.store(params, et);
-      epilogue_sync<R::kEpiThreads>();
-      const int next = tile + gridDim.x;
-      if (next < total_tiles) tp.fetch(p, (next % p.n_tiles) * kOutCols, et);
+      if constexpr (kParams) {
+        epilogue_sync<R::kEpiThreads>();
+        tp.store(params, et);
+        epilogue_sync<R::kEpiThreads>();
+        const int next = tile + gridDim.x;
+        if (next < total_tiles) tp.fetch(p, (next % p.n_tiles) * kOutCols, et);
+      }
       if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
       const int m = m0 + row_in_tile;
@@ -619,6 +762,26 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         }
         const int col = (g0 + g) * 32;           // first output column of this group, tile-relative
         const int n = n0 + col;
+        if constexpr (kOut == OUT_NVFP4) {
+          // codes [M, N/2]; scales in the tensor-core layout of an [M, N] operand
+          uint4 q;
+          const uint32_t sf2 =
+              swiglu_nvfp4_group(ca, cb, p.a_scale, p.alpha_up, p.q_scale, __fmul_rn(6.f, p.q_scale), q);
+          if (row_ok) {
+            *reinterpret_cast<uint4*>(p.q_codes + static_cast<int64_t>(m) * (p.N / 2) + n / 2) = q;
+            const int64_t sf_off = (static_cast<int64_t>(m >> 7) * (p.N / 64) + (n >> 6)) * kSfChunk +
+                                   (m & 31) * 16 + ((m >> 5) & 3) * 4 + ((n >> 4) & 3);
+            *reinterpret_cast<uint16_t*>(p.q_sf + sf_off) = static_cast<uint16_t>(sf2);
+          }
+          if (g + 1 < kGroups) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              ca[j] = na[j];
+              cb[j] = nb[j];
+            }
+          }
+          continue;
+        }
         float v[32];
         if constexpr (kEpi == EPI_SCALE) {
           if (p.a_scale_rows != nullptr) scale_group<kInt8, true>(ca, sa, params + col, params + 256 + col, v);

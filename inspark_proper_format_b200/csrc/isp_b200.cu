@@ -97,11 +97,19 @@ constexpr int kStages = ISP_GEMM_STAGES;
 constexpr int kScaleEpiWarps = ISP_GEMM_SCALE_EPI_WARPS;   // scale/bias/residual epilogues
 constexpr int kSwigluEpiWarps = 4;                         // SwiGLU: 128 output columns per tile
 
-template <int kBN, int kStages, int kEpiWarps, bool kInt8, int kEpi, int kOut>
+// NVFP4: 128 x 128 tiles (two 128-column accumulators + 32 scale columns per
+// stage in TMEM); a stage is 16 KB of A, 16 KB of B and 4 KB of scales.
+#ifndef ISP_GEMM_FP4_STAGES
+#define ISP_GEMM_FP4_STAGES 5
+#endif
+constexpr int kFp4BN = 128;
+constexpr int kFp4Stages = ISP_GEMM_FP4_STAGES;
+
+template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, const CUtensorMap& o,
            const Params& p, cudaStream_t stream) {
-  auto kern = gemm_kernel<kBN, kStages, kEpiWarps, kInt8, kEpi, kOut>;
-  constexpr int kSmem = Smem<kBN, kStages, kEpiWarps>::kBytes;
+  auto kern = gemm_kernel<kBN, kStages, kEpiWarps, kAB, kEpi, kOut>;
+  constexpr int kSmem = Smem<kBN, kStages, kEpiWarps, kAB == AB_FP4 ? kSfStageBytes : 0>::kBytes;
   static_assert(kSmem <= 232448, "shared memory budget of one sm_100 CTA");
   static bool configured[64] = {false};
   int dev = 0;
@@ -117,16 +125,40 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, co
   return launch_status();
 }
 
-template <bool kInt8>
+template <int kAB>
 int dispatch_scale_out(int out_kind, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
                        const Params& p, cudaStream_t s) {
   switch (out_kind) {
-    case OUT_BF16: return launch<kBN, kStages, kScaleEpiWarps, kInt8, EPI_SCALE, OUT_BF16>(a, b, b, o, p, s);
-    case OUT_F16: return launch<kBN, kStages, kScaleEpiWarps, kInt8, EPI_SCALE, OUT_F16>(a, b, b, o, p, s);
-    case OUT_F32: return launch<kBN, kStages, kScaleEpiWarps, kInt8, EPI_SCALE, OUT_F32>(a, b, b, o, p, s);
-    case OUT_E4M3: return launch<kBN, kStages, kScaleEpiWarps, kInt8, EPI_SCALE, OUT_E4M3>(a, b, b, o, p, s);
+    case OUT_BF16: return launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, OUT_BF16>(a, b, b, o, p, s);
+    case OUT_F16: return launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, OUT_F16>(a, b, b, o, p, s);
+    case OUT_F32: return launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, OUT_F32>(a, b, b, o, p, s);
+    case OUT_E4M3: return launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, OUT_E4M3>(a, b, b, o, p, s);
     default: return ISP_ERR_DTYPE;
   }
+}
+
+int dispatch_fp4_scale_out(int out_kind, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
+                           const Params& p, cudaStream_t s) {
+  switch (out_kind) {
+    case OUT_BF16: return launch<kFp4BN, kFp4Stages, kScaleEpiWarps, AB_FP4, EPI_SCALE, OUT_BF16>(a, b, b, o, p, s);
+    case OUT_F16: return launch<kFp4BN, kFp4Stages, kScaleEpiWarps, AB_FP4, EPI_SCALE, OUT_F16>(a, b, b, o, p, s);
+    case OUT_F32: return launch<kFp4BN, kFp4Stages, kScaleEpiWarps, AB_FP4, EPI_SCALE, OUT_F32>(a, b, b, o, p, s);
+    default: return ISP_ERR_DTYPE;
+  }
+}
+
+bool global_scale_ok(float g) { return g >= 0x1p-100f && g <= 0x1p100f; }
+
+// Row-major E4M3 scales [R, K/16] -> tensor-core layout; one thread per
+// 4-byte word (the 4 scales of one row in one 64-element K chunk).
+__global__ void scales_to_mma_kernel(const uint32_t* src, int64_t R, int kchunks, uint32_t* dst, int64_t words) {
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (w >= words) return;
+  const int64_t r = w / kchunks;
+  const int c = static_cast<int>(w - r * kchunks);
+  const uint32_t v = r < R ? __ldg(src + r * kchunks + c) : 0u;
+  const int64_t off = ((r >> 7) * kchunks + c) * 128 + (r & 31) * 4 + ((r >> 5) & 3);   // in words
+  dst[off] = v;
 }
 
 int out_kind_of(int dtype) {
@@ -184,12 +216,14 @@ int isp_norm_quant(const void* x, int x_dtype, int64_t M, int K, const float* ga
   if (x_dtype != ISP_BF16 && x_dtype != ISP_F32) return ISP_ERR_DTYPE;
   if (M < 0 || K <= 0 || K % 16 != 0) return ISP_ERR_SHAPE;
   if (norm_kind < ISP_NORM_NONE || norm_kind > ISP_NORM_BIAS) return ISP_ERR_ARG;
-  if (qfmt < ISP_Q_E4M3_STATIC || qfmt > ISP_Q_NVFP4) return ISP_ERR_ARG;
+  if (qfmt < ISP_Q_E4M3_STATIC || qfmt > ISP_Q_NVFP4_MMA) return ISP_ERR_ARG;
+  const bool nvfp4 = qfmt == ISP_Q_NVFP4 || qfmt == ISP_Q_NVFP4_MMA;
+  if (qfmt == ISP_Q_NVFP4_MMA && K % 64 != 0) return ISP_ERR_SHAPE;
   if ((norm_kind == ISP_NORM_RMS_GPTFAST || norm_kind == ISP_NORM_RMS_QWEN) && gamma == nullptr)
     return ISP_ERR_ARG;
   if (norm_kind == ISP_NORM_BIAS && bias == nullptr) return ISP_ERR_ARG;
-  if ((qfmt == ISP_Q_E4M3_ROW || qfmt == ISP_Q_NVFP4) && scales_out == nullptr) return ISP_ERR_ARG;
-  if (qfmt != ISP_Q_E4M3_ROW && !(scale > 0.f)) return ISP_ERR_ARG;
+  if ((qfmt == ISP_Q_E4M3_ROW || nvfp4) && scales_out == nullptr) return ISP_ERR_ARG;
+  if (qfmt != ISP_Q_E4M3_ROW && !isp::gemm::global_scale_ok(scale)) return ISP_ERR_ARG;
   if (!isp::aligned16(x) || !isp::aligned16(codes)) return ISP_ERR_ALIGN;
   if ((gamma && !isp::aligned16(gamma)) || (bias && !isp::aligned16(bias)) ||
       (smooth && !isp::aligned16(smooth)))
@@ -292,8 +326,8 @@ int isp_scaled_gemm(const void* A, const void* W, int ab_dtype, int64_t M, int N
   p.out_inv = out_inv_scale;
   p.out2 = out2;
   p.out2_inv = out2_inv_scale;
-  return ab_dtype == ISP_I8 ? dispatch_scale_out<true>(out_kind, ta, tb, to, p, stream)
-                            : dispatch_scale_out<false>(out_kind, ta, tb, to, p, stream);
+  return ab_dtype == ISP_I8 ? dispatch_scale_out<AB_I8>(out_kind, ta, tb, to, p, stream)
+                            : dispatch_scale_out<AB_E4M3>(out_kind, ta, tb, to, p, stream);
 }
 
 int isp_gated_up(const void* A, const void* W1, const void* W3, int interleaved, int64_t M, int N, int K,
@@ -336,11 +370,99 @@ int isp_gated_up(const void* A, const void* W1, const void* W3, int interleaved,
   p.out_scale = out_scale;
   if (interleaved) {
     return out_kind == OUT_E4M3
-               ? launch<kBN, kStages, kSwigluEpiWarps, false, EPI_SWIGLU_INTERLEAVED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
-               : launch<kBN, kStages, kSwigluEpiWarps, false, EPI_SWIGLU_INTERLEAVED, OUT_F32>(ta, tb, tb2, to, p, stream);
+               ? launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_INTERLEAVED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
+               : launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_INTERLEAVED, OUT_F32>(ta, tb, tb2, to, p, stream);
   }
-  return out_kind == OUT_E4M3 ? launch<kBN, kStages, kSwigluEpiWarps, false, EPI_SWIGLU_PAIRED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
-                              : launch<kBN, kStages, kSwigluEpiWarps, false, EPI_SWIGLU_PAIRED, OUT_F32>(ta, tb, tb2, to, p, stream);
+  return out_kind == OUT_E4M3 ? launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
+                              : launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_F32>(ta, tb, tb2, to, p, stream);
+}
+
+int isp_nvfp4_scales_to_mma(const void* src, int64_t R, int K, void* dst, isp_stream_t stream) {
+  if (src == nullptr || dst == nullptr) return ISP_ERR_ARG;
+  if (R < 0 || K <= 0 || K % 64 != 0 || R > (int64_t(1) << 40)) return ISP_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(src) & 3) || (reinterpret_cast<uintptr_t>(dst) & 3)) return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  if (R == 0) return ISP_OK;
+  const int kchunks = K / 64;
+  const int64_t words = (R + 127) / 128 * 128 * kchunks;
+  const unsigned grid = static_cast<unsigned>((words + 255) / 256);
+  isp::gemm::scales_to_mma_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint32_t*>(src), R, kchunks,
+                                                           static_cast<uint32_t*>(dst), words);
+  return isp::launch_status();
+}
+
+int isp_nvfp4_gemm(const void* A, const void* A_sf, const void* W, const void* W_sf, int64_t M, int N, int K,
+                   float alpha, const float* bias, const void* residual, int residual_dtype, void* out, int out_dtype,
+                   isp_stream_t stream) {
+  using namespace isp::gemm;
+  if (!A || !A_sf || !W || !W_sf || !out) return ISP_ERR_ARG;
+  if (out_dtype != ISP_BF16 && out_dtype != ISP_F16 && out_dtype != ISP_F32) return ISP_ERR_DTYPE;
+  if (residual != nullptr && residual_dtype != ISP_F32 && residual_dtype != ISP_BF16) return ISP_ERR_DTYPE;
+  if (!(alpha == alpha) || alpha == INFINITY || alpha == -INFINITY) return ISP_ERR_ARG;
+  if (M < 0 || M > 0x7FFFFFFFll || N <= 0 || K <= 0 || K % 64 != 0 || N % 8 != 0) return ISP_ERR_SHAPE;
+  if (!isp::aligned16(A) || !isp::aligned16(W) || !isp::aligned16(A_sf) || !isp::aligned16(W_sf) ||
+      !isp::aligned16(out) || (bias && !isp::aligned16(bias)))
+    return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  if (M == 0) return ISP_OK;
+  const int out_kind = out_kind_of(out_dtype);
+  CUtensorMap ta, tb, to;
+  if (!make_map(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, M, kBK, kBM) ||
+      !make_map(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, kBK, kFp4BN) ||
+      !make_out_map(&to, out, out_kind, M, N))
+    return ISP_ERR_ALIGN;
+  Params p{};
+  p.M = static_cast<int>(M);
+  p.N = N;
+  p.K = K;
+  p.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  p.n_tiles = (N + kFp4BN - 1) / kFp4BN;
+  p.k_blocks = (K / 2 + kBK - 1) / kBK;
+  p.k_chunks = K / 64;
+  p.sfa = static_cast<const uint8_t*>(A_sf);
+  p.sfb = static_cast<const uint8_t*>(W_sf);
+  p.a_scale = alpha;
+  p.bias = bias;
+  p.residual = residual;
+  p.residual_f32 = residual_dtype == ISP_F32;
+  return dispatch_fp4_scale_out(out_kind, ta, tb, to, p, stream);
+}
+
+int isp_nvfp4_gated_up(const void* A, const void* A_sf, const void* W13, const void* W13_sf, int64_t M, int N, int K,
+                       float alpha_gate, float alpha_up, float h_scale, void* h_codes, void* h_sf,
+                       isp_stream_t stream) {
+  using namespace isp::gemm;
+  if (!A || !A_sf || !W13 || !W13_sf || !h_codes || !h_sf) return ISP_ERR_ARG;
+  if (!(alpha_gate == alpha_gate) || !(alpha_up == alpha_up) || alpha_gate == INFINITY || alpha_gate == -INFINITY ||
+      alpha_up == INFINITY || alpha_up == -INFINITY || !global_scale_ok(h_scale))
+    return ISP_ERR_ARG;
+  if (M < 0 || M > 0x7FFFFFFFll || N <= 0 || K <= 0 || K % 64 != 0 || N % 64 != 0) return ISP_ERR_SHAPE;
+  if (!isp::aligned16(A) || !isp::aligned16(W13) || !isp::aligned16(A_sf) || !isp::aligned16(W13_sf) ||
+      !isp::aligned16(h_codes) || !isp::aligned16(h_sf))
+    return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  if (M == 0) return ISP_OK;
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, M, kBK, kBM) ||
+      !make_map(&tb, W13, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, 2ull * N, kBK, kFp4BN))
+    return ISP_ERR_ALIGN;
+  Params p{};
+  p.M = static_cast<int>(M);
+  p.N = N;
+  p.K = K;
+  p.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  p.n_tiles = N / (kFp4BN / 2);
+  p.k_blocks = (K / 2 + kBK - 1) / kBK;
+  p.k_chunks = K / 64;
+  p.sfa = static_cast<const uint8_t*>(A_sf);
+  p.sfb = static_cast<const uint8_t*>(W13_sf);
+  p.a_scale = alpha_gate;
+  p.alpha_up = alpha_up;
+  p.q_scale = h_scale;
+  p.q_codes = static_cast<uint8_t*>(h_codes);
+  p.q_sf = static_cast<uint8_t*>(h_sf);
+  // The output map is unused by the NVFP4 epilogue (direct stores); pass A's.
+  return launch<kFp4BN, kFp4Stages, kScaleEpiWarps, AB_FP4, EPI_SWIGLU_PAIRED, OUT_NVFP4>(ta, tb, tb, ta, p, stream);
 }
 
 }  // extern "C"

@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
       if (lane == 0) static_cast<float*>(p.scales_out)[row] = s;
     }
     uint8_t* out = static_cast<uint8_t*>(p.codes) + row * K;
+    const float rs = __frcp_rn(s);
 #pragma unroll
     for (int i = 0; i < kGroups; ++i) {
       const int g = lane + 32 * i;
@@ -150,8 +151,8 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
         for (int h = 0; h < 2; ++h) {
           const float* q = &v[i][4 * h];
           // satfinite == the reference's clamp(-448, 448) before the cast (NaN stays NaN)
-          uint32_t lo = e4m3x2(__fdiv_rn(q[0], s), __fdiv_rn(q[1], s));
-          uint32_t hi = e4m3x2(__fdiv_rn(q[2], s), __fdiv_rn(q[3], s));
+          uint32_t lo = e4m3x2(div_rn_recip(q[0], s, rs), div_rn_recip(q[1], s, rs));
+          uint32_t hi = e4m3x2(div_rn_recip(q[2], s, rs), div_rn_recip(q[3], s, rs));
           w[h] = lo | (hi << 16);
         }
         *reinterpret_cast<uint2*>(out + g * 8) = make_uint2(w[0], w[1]);
@@ -159,6 +160,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
     }
   } else if constexpr (kFmt == ISP_Q_INT8_STATIC) {
     int8_t* out = static_cast<int8_t*>(p.codes) + row * K;
+    const float rscale = __frcp_rn(p.scale);
 #pragma unroll
     for (int i = 0; i < kGroups; ++i) {
       const int g = lane + 32 * i;
@@ -170,15 +172,21 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
         for (int j = 0; j < 8; ++j) {
           float y = v[i][j];
           if (p.smooth != nullptr) y = __fdiv_rn(y, sm[j]);
-          const int8_t q = int8_rne_sat(__fdiv_rn(y, p.scale));
+          const int8_t q = int8_rne_sat(div_rn_recip(y, p.scale, rscale));
           w[j >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(q)) << (8 * (j & 3));
         }
         *reinterpret_cast<uint2*>(out + g * 8) = make_uint2(w[0], w[1]);
       }
     }
-  } else {  // ISP_Q_NVFP4: lanes (2p, 2p+1) hold the two halves of one 16-element block
+  } else {  // NVFP4: lanes (2p, 2p+1) hold the two halves of one 16-element block
     uint8_t* out = static_cast<uint8_t*>(p.codes) + row * (K / 2);
-    uint8_t* sf = static_cast<uint8_t*>(p.scales_out) + row * (K / 16);
+    // Row-major [M, K/16] scales, or the tensor-core layout (128-row x 4-block
+    // chunks of 512 bytes, K chunks first): block b of row m sits at
+    // ((m/128)*(K/64) + b/4)*512 + (m%32)*16 + ((m%128)/32)*4 + b%4.
+    uint8_t* sf = kFmt == ISP_Q_NVFP4
+                      ? static_cast<uint8_t*>(p.scales_out) + row * (K / 16)
+                      : static_cast<uint8_t*>(p.scales_out) + (row >> 7) * (K / 64) * 512 + (row & 31) * 16 +
+                            ((row >> 5) & 3) * 4;
     const float gscale = p.scale;
     const float six_g = __fmul_rn(6.f, gscale);
 #pragma unroll
@@ -196,11 +204,16 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
         const uint16_t sc2 = e4m3x2(fminf(sb, 448.f), 0.f);
         const uint8_t sc = static_cast<uint8_t>(sc2 & 0xFF);
         const float denom = __fmul_rn(e4m3_to_f32(sc), gscale);
+        const float rden = __frcp_rn(denom);
         uint32_t packed = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) packed |= e2m1_code(__fdiv_rn(v[i][j], denom)) << (4 * j);
+        for (int j = 0; j < 8; ++j) packed |= e2m1_code(div_rn_recip(v[i][j], denom, rden)) << (4 * j);
         *reinterpret_cast<uint32_t*>(out + g * 4) = packed;
-        if ((g & 1) == 0) sf[g >> 1] = sc;
+        if ((g & 1) == 0) {
+          const int b = g >> 1;
+          if constexpr (kFmt == ISP_Q_NVFP4) sf[b] = sc;
+          else sf[(b >> 2) * 512 + (b & 3)] = sc;
+        }
       }
     }
   }
@@ -230,6 +243,7 @@ int launch_norm_quant_fmt(int fmt, const NormQuantParams& p, cudaStream_t s) {
     case ISP_Q_E4M3_ROW: return launch_norm_quant_groups<kBF16, kNorm, ISP_Q_E4M3_ROW>(p, s);
     case ISP_Q_INT8_STATIC: return launch_norm_quant_groups<kBF16, kNorm, ISP_Q_INT8_STATIC>(p, s);
     case ISP_Q_NVFP4: return launch_norm_quant_groups<kBF16, kNorm, ISP_Q_NVFP4>(p, s);
+    case ISP_Q_NVFP4_MMA: return launch_norm_quant_groups<kBF16, kNorm, ISP_Q_NVFP4_MMA>(p, s);
     default: return ISP_ERR_ARG;
   }
 }

@@ -14,7 +14,13 @@ from . import _lib
 KINDS = {"none": _lib.NORM_NONE, "rms_gptfast": _lib.NORM_RMS_GPTFAST,
          "rms_qwen": _lib.NORM_RMS_QWEN, "bias": _lib.NORM_BIAS}
 FORMATS = {"e4m3": _lib.Q_E4M3_STATIC, "e4m3_row": _lib.Q_E4M3_ROW,
-           "int8": _lib.Q_INT8_STATIC, "nvfp4": _lib.Q_NVFP4}
+           "int8": _lib.Q_INT8_STATIC, "nvfp4": _lib.Q_NVFP4, "nvfp4_mma": _lib.Q_NVFP4_MMA}
+
+
+def mma_scale_bytes(rows: int, k: int) -> int:
+    """Bytes of NVFP4 block scales of an [rows, k] operand in the tensor-core
+    layout (128-row x 4-block chunks of 512 bytes, rows padded to 128)."""
+    return (rows + 127) // 128 * 128 * (k // 16)
 
 
 def _param(t, k, name):
@@ -38,7 +44,10 @@ def norm_quant(x: torch.Tensor, *, kind: str = "rms_gptfast", fmt: str = "e4m3",
       * ``e4m3_row``: codes and FP32 per-row scales ``max(amax/448, 1e-12)``;
       * ``int8``: int8 codes of ``clamp(rne(y / smooth / scale))``, scales None;
       * ``nvfp4``: uint8 [..., K/2] packed E2M1 (low nibble = even k) and
-        float8_e4m3fn [..., K/16] block scales, with ``global_scale`` g.
+        float8_e4m3fn [..., K/16] block scales, with ``global_scale`` g;
+      * ``nvfp4_mma``: the same codes, the block scales as a flat uint8 tensor
+        in the tensor-core layout that ``nvfp4.nvfp4_gemm`` consumes
+        (``mma_scale_bytes(M, K)`` bytes; K % 64 == 0).
     """
     if kind not in KINDS or fmt not in FORMATS:
         raise ValueError(f"unknown norm kind {kind!r} or format {fmt!r}")
@@ -57,13 +66,17 @@ def norm_quant(x: torch.Tensor, *, kind: str = "rms_gptfast", fmt: str = "e4m3",
         ls = log_scale if isinstance(log_scale, torch.Tensor) else torch.tensor(float(log_scale or 0.0))
         out_mul = float(ls.detach().float().exp())
     lead = x.shape[:-1]
-    if fmt == "nvfp4":
+    if fmt in ("nvfp4", "nvfp4_mma"):
         if global_scale is None:
             raise ValueError("nvfp4 needs the FP32 global scale")
         s = float(global_scale)
         codes = out if out is not None else torch.empty(*lead, k // 2, device=x.device, dtype=torch.uint8)
-        scales = scales_out if scales_out is not None else torch.empty(*lead, k // 16, device=x.device,
-                                                                      dtype=torch.float8_e4m3fn)
+        if scales_out is not None:
+            scales = scales_out
+        elif fmt == "nvfp4":
+            scales = torch.empty(*lead, k // 16, device=x.device, dtype=torch.float8_e4m3fn)
+        else:
+            scales = torch.zeros(mma_scale_bytes(m, k), device=x.device, dtype=torch.uint8)
     else:
         if fmt in ("e4m3", "int8"):
             if scale is None:

@@ -76,5 +76,30 @@ def gated_up_nvfp4(a_packed, a_scodes, g_a, w1, w3, out_global_scale):
     return packed, scodes, h
 
 
+def sf_to_mma_layout(sf: np.ndarray) -> np.ndarray:
+    """Block scales [R, K/16] (row-major, ModelOpt order) -> the tensor-core
+    layout: 128-row x 4-block chunks of 512 bytes, K-chunks first, with byte
+    ((r//128) * (K/64) + k16//4) * 512 + (r%32)*16 + ((r%128)//32)*4 + k16%4.
+    Rows are padded to a multiple of 128 with zero bytes."""
+    sf = np.asarray(sf, np.uint8)
+    r, kb = sf.shape
+    if kb % 4:
+        raise ValueError("K must be a multiple of 64")
+    rb = (r + 127) // 128
+    out = np.zeros(rb * 128 * kb, np.uint8)
+    rows = np.arange(r)[:, None]
+    ks = np.arange(kb)[None, :]
+    off = ((rows // 128) * (kb // 4) + ks // 4) * 512 + (rows % 32) * 16 + ((rows % 128) // 32) * 4 + ks % 4
+    out[off] = sf
+    return out
+
+
+def sf_from_mma_layout(tiled: np.ndarray, r: int, kb: int) -> np.ndarray:
+    rows = np.arange(r)[:, None]
+    ks = np.arange(kb)[None, :]
+    off = ((rows // 128) * (kb // 4) + ks // 4) * 512 + (rows % 32) * 16 + ((rows % 128) // 32) * 4 + ks % 4
+    return np.asarray(tiled, np.uint8)[off]
+
+
 def e4m3_static(h: np.ndarray, scale: float) -> np.ndarray:
     return e4m3_encode(np.clip((h / np.float32(scale)).astype(np.float32), -E4M3_MAX, E4M3_MAX))
