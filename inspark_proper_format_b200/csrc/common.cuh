@@ -62,6 +62,15 @@ ISP_D uint32_t e2m1_code(float v) {
   return m | (v < 0.f ? 8u : 0u);
 }
 
+// Two E2M1 codes from the hardware conversion (round to nearest even,
+// saturating to +-6): `lo` in bits 0-3, `hi` in bits 4-7.  Matches e2m1_code
+// on every finite input except -0.0 (hardware: 0x8); callers pass +-0 as +0.
+ISP_D uint32_t e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n .reg .b8 t;\n cvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n cvt.u32.u8 %0, t;\n}" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // RN(x / d) from a reciprocal y = RN(1/d) shared by many quotients (one
 // reciprocal per scale instead of one division per element).  Markstein's
 // correction (P. Markstein, IBM J. Res. Dev. 34(1), 1990; Muller et al.,

@@ -85,18 +85,34 @@ struct Params {
   uint8_t* q_sf;          // NVFP4 output: block scales, tensor-core layout
 };
 
-template <int kBN, int kStages, int kEpiWarps, int kSfBytes = 0>
+// Shared-memory layout.  Streaming (kBStatK == 0): stage s = [A | B | A scales | B scales].
+// B-stationary (kBStatK > 0 bytes of K): stage s = [A | A scales], then the resident
+// B tile (kBStatK / 128 boxes of kBN rows x 128 B) and its scales, loaded once per
+// N tile.  Scales exist for NVFP4 only; every swizzled region starts 1024-aligned.
+template <int kBN, int kStages, int kEpiWarps, bool kFp4, bool kStaging, int kBStatK>
 struct Smem {
+  static constexpr bool kStat = kBStatK > 0;
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = kBN * kBK;
-  static constexpr int kStageBytes = kABytes + kBBytes + kSfBytes;   // [A | B | A scales | B scales]
-  static constexpr int ab(int s) { return s * kStageBytes; }
-  static constexpr int sf(int s) { return s * kStageBytes + kABytes + kBBytes; }
-  static constexpr int kStagingBytes = kEpiWarps * kStagingBufs * 32 * 128;  // per warp: buffers of 32 rows x 128 B
-  static constexpr int kParamOffset = kStages * kStageBytes + kStagingBytes;
+  static constexpr int kSf = kFp4 ? kSfOperandBytes : 0;
+  static constexpr int kStageBytes = kStat ? kABytes + kSf : kABytes + kBBytes + 2 * kSf;
+  static constexpr int a(int s) { return s * kStageBytes; }
+  static constexpr int b(int s) { return s * kStageBytes + kABytes; }                 // streaming
+  static constexpr int sfa(int s) { return s * kStageBytes + kABytes + (kStat ? 0 : kBBytes); }
+  static constexpr int sfb(int s) { return sfa(s) + kSf; }                             // streaming
+  static constexpr int kBResOffset = kStages * kStageBytes;
+  static constexpr int kBResBytes = kStat ? kBN * kBStatK : 0;
+  static constexpr int kSfbResOffset = kBResOffset + kBResBytes;
+  static constexpr int kSfbResBytes = (kStat && kFp4) ? (2 * kBStatK / 64) * kSfChunk : 0;
+  static constexpr int kStagingOffset = kSfbResOffset + kSfbResBytes;
+  // per epilogue warp: buffers of 32 rows x 128 B for the TMA stores (none for direct-store epilogues)
+  static constexpr int kStagingBytes = kStaging ? kEpiWarps * kStagingBufs * 32 * 128 : 0;
+  static constexpr int kParamOffset = kStagingOffset + kStagingBytes;
   static constexpr int kParamBytes = 512 * 4;              // per-tile column scales / bias
   static constexpr int kBarOffset = kParamOffset + kParamBytes;
   static constexpr int kBytes = kBarOffset + 256;          // + barriers/flags (base is 1024-aligned)
+  static_assert(kStageBytes % 1024 == 0 && kBResOffset % 1024 == 0 && kStagingOffset % 1024 == 0,
+                "swizzled regions start 1024-byte aligned");
 };
 
 // ----------------------------------------------------------------------------
@@ -138,6 +154,30 @@ ISP_D bool wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag
         *abort_flag = 1;
         return false;
       }
+    }
+  }
+}
+
+// Bounded wait for a converged warp: every lane polls, lane 0's result decides,
+// and the warp leaves together (a lone polling lane whose warp-mates are parked
+// at a block barrier throttles the tcgen05 issue stream it feeds).
+ISP_D bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (__shfl_sync(0xffffffffu, static_cast<int>(mbar_try_wait(bar, parity)), 0)) return true;
+  const uint64_t start = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (__shfl_sync(0xffffffffu, static_cast<int>(mbar_try_wait(bar, parity)), 0)) return true;
+    if ((i & 63u) == 0) {
+      int stop = 0;
+      if ((threadIdx.x & 31) == 0) {
+        if (*abort_flag) {
+          stop = 1;
+        } else if (globaltimer() - start > kWaitLimitNs) {
+          record_timeout();
+          *abort_flag = 1;
+          stop = 1;
+        }
+      }
+      if (__shfl_sync(0xffffffffu, stop, 0)) return false;
     }
   }
 }
@@ -257,7 +297,26 @@ ISP_D void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 32 TMEM lanes x 16 consecutive 32-bit columns -> 16 registers per thread.
+ISP_D void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 ISP_D void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+ISP_D void tmem_ld_wait(uint32_t (&r)[16], uint32_t (&s)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(s[0]), "+r"(s[1]), "+r"(s[2]), "+r"(s[3]), "+r"(s[4]), "+r"(s[5]),
+                 "+r"(s[6]), "+r"(s[7]), "+r"(s[8]), "+r"(s[9]), "+r"(s[10]), "+r"(s[11]), "+r"(s[12]),
+                 "+r"(s[13]), "+r"(s[14]), "+r"(s[15])
+               :
+               : "memory");
+}
 // Wait for outstanding tcgen05.ld and tie the loaded registers to the wait, so
 // no use of them can be scheduled before it.
 ISP_D void tmem_ld_wait(uint32_t (&r)[32]) {
@@ -498,59 +557,120 @@ ISP_D void swiglu_group(const uint32_t (&a)[32], const uint32_t (&b)[32], const 
   }
 }
 
-// NVFP4 SwiGLU of one 32-output group of one row:
+// NVFP4 SwiGLU of one 16-output block of one row (one NVFP4 scale block):
 //   h = silu(acc_gate * alpha_gate) * (acc_up * alpha_up)
-// quantized as two 16-element blocks with the global scale gq:
-//   s = e4m3(min(amax / (6 gq), 448)) (an all-zero block takes s = 1),
+// quantized with the global scale gq:
+//   s = e4m3(min(amax(h) / (6 gq), 448)) (an all-zero block takes s = 1),
 //   code = e2m1(h / (s gq)), low nibble = even column.
-// The codes go to `codes` (16 bytes); the two scale bytes are returned.
-ISP_D uint32_t swiglu_nvfp4_group(const uint32_t (&a)[32], const uint32_t (&b)[32], float ag, float au, float gq,
-                                  float six_gq, uint4& codes) {
-  float h[32];
+// silu(g) = g/2 * (1 + tanh(g/2)) takes one MUFU op per element, and alpha_up
+// is applied once per block: h' = silu(g) * acc_up, amax(h) = amax(h') |alpha_up|,
+// h / (s gq) = h' * RN(alpha_up / (s gq)).  The quotient can therefore differ
+// from an exactly rounded h / (s gq) by an ulp or two, which moves a code only
+// within that distance of a decision point.  A block whose scale rounds to 0
+// takes the codes of h / 0: +-6 for h != 0, 0 for h == 0.
+// ag_half = alpha_gate / 2; r6 = RN(1 / (6 gq)).  Returns the 8 code bytes
+// (low word = columns 0-7) and the scale byte in `sf`.
+ISP_D float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+ISP_D uint2 swiglu_nvfp4_block(const uint32_t (&a)[16], const uint32_t (&b)[16], float ag_half, float au, float gq,
+                               float six_gq, float r6, uint32_t& sf) {
+  float h[16];
+  float amax = 0.f;
 #pragma unroll
-  for (int j = 0; j < 32; ++j)
-    h[j] = silu_mul(__fmul_rn(__uint_as_float(a[j]), ag), __fmul_rn(__uint_as_float(b[j]), au));
-  uint32_t w[4];
-  uint32_t sf = 0;
-#pragma unroll
-  for (int blk = 0; blk < 2; ++blk) {
-    float amax = 0.f;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(h[16 * blk + j]));
-    float sb = __fdiv_rn(amax, six_gq);
-    if (sb == 0.f) sb = 1.f;
-    const uint32_t sc = e4m3x2(fminf(sb, 448.f), 0.f) & 0xFFu;
-    const float denom = __fmul_rn(e4m3_to_f32(static_cast<uint8_t>(sc)), gq);
-    const float rden = __frcp_rn(denom);
+  for (int j = 0; j < 16; ++j) {
+    const float hg = __fmul_rn(__uint_as_float(a[j]), ag_half);
+    h[j] = __fmul_rn(__fmaf_rn(hg, tanh_approx(hg), hg), __uint_as_float(b[j]));
+    amax = fmaxf(amax, fabsf(h[j]));
+  }
+  float sb = div_rn_recip(__fmul_rn(amax, fabsf(au)), six_gq, r6);
+  if (sb == 0.f) sb = 1.f;
+  const uint32_t sc = e4m3x2(fminf(sb, 448.f), 0.f) & 0xFFu;
+  sf = sc;
+  uint32_t w[2];
+  if (sc != 0u) {
+    const float r = __fmul_rn(au, __frcp_rn(__fmul_rn(e4m3_to_f32(static_cast<uint8_t>(sc)), gq)));
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       uint32_t packed = 0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        packed |= e2m1_code(div_rn_recip(h[16 * blk + 8 * half + j], denom, rden)) << (4 * j);
-      w[2 * blk + half] = packed;
+      for (int j = 0; j < 8; j += 2) {
+        const float* hp = &h[8 * half + j];
+        // fma(h, r, +0) == RN(h r) and turns -0 into +0
+        packed |= e2m1x2(__fmaf_rn(hp[0], r, 0.f), __fmaf_rn(hp[1], r, 0.f)) << (4 * j);
+      }
+      w[half] = packed;
     }
-    sf |= sc << (8 * blk);
+  } else {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t packed = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float v = __fmul_rn(h[8 * half + j], au);
+        packed |= (v > 0.f ? 7u : (v < 0.f ? 15u : 0u)) << (4 * j);
+      }
+      w[half] = packed;
+    }
   }
-  codes = make_uint4(w[0], w[1], w[2], w[3]);
-  return sf;
+  return make_uint2(w[0], w[1]);
 }
+
+// ----------------------------------------------------------------------------
+// Tile schedule
+// ----------------------------------------------------------------------------
+// Streaming: CTA c takes tiles c, c + grid, ... in M-major order (all CTAs work
+// on neighbouring tiles, so A and B re-reads hit L2).  B-stationary: CTA c takes
+// a contiguous range of the N-major order, so it crosses at most a few N tiles
+// and reloads its resident B tile only there.
+template <bool kStat>
+struct Schedule {
+  int begin, end, step;
+  ISP_D Schedule(const Params& p) {
+    const int total = p.m_tiles * p.n_tiles;
+    if constexpr (kStat) {
+      begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * total / gridDim.x);
+      end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x);
+      step = 1;
+    } else {
+      begin = blockIdx.x;
+      end = total;
+      step = gridDim.x;
+    }
+  }
+  ISP_D static void coords(const Params& p, int t, int& mt, int& nt) {
+    if constexpr (kStat) {
+      nt = t / p.m_tiles;
+      mt = t - nt * p.m_tiles;
+    } else {
+      mt = t / p.n_tiles;
+      nt = t - mt * p.n_tiles;
+    }
+  }
+};
 
 // ----------------------------------------------------------------------------
 // The kernel
 // ----------------------------------------------------------------------------
-template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut>
+// kBStatK > 0: B-stationary schedule holding kBStatK bytes of K of the B tile
+// resident (requires K bytes <= kBStatK).
+template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut, int kBStatK>
 __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_out,
                 const Params p) {
   constexpr bool kInt8 = kAB == AB_I8;
   constexpr bool kFp4 = kAB == AB_FP4;
+  constexpr bool kStat = kBStatK > 0;
   static_assert(!kFp4 || kBN == 128, "NVFP4 tiles are 128 x 128 (one scale chunk per operand and K = 64)");
   static_assert(kOut != OUT_NVFP4 || (kFp4 && kEpi == EPI_SWIGLU_PAIRED), "NVFP4 output is the FP4 SwiGLU epilogue");
-  using L = Smem<kBN, kStages, kEpiWarps, kFp4 ? kSfStageBytes : 0>;
-  static_assert(L::kStageBytes % 1024 == 0, "every stage's swizzled A/B tiles start 1024-byte aligned");
+  static_assert(kBStatK % kBK == 0, "resident K is whole 128-byte blocks");
+  using L = Smem<kBN, kStages, kEpiWarps, kFp4, kOut != OUT_NVFP4, kBStatK>;
   using R = Roles<kEpiWarps>;
+  using S = Schedule<kStat>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // The 128-byte swizzle patterns assume a 1024-byte aligned base; refuse to run otherwise.
   if ((smem_u32(smem_raw) & 1023u) != 0) {
@@ -558,21 +678,26 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     return;
   }
   uint8_t* smem = smem_raw;
-  uint8_t* staging = smem + kStages * L::kStageBytes;
+  uint8_t* staging = smem + L::kStagingOffset;
   float* params = reinterpret_cast<float*>(smem + L::kParamOffset);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* empty_bar = full_bar + kStages;
   uint64_t* tfull_bar = empty_bar + kStages;     // [2]
   uint64_t* tempty_bar = tfull_bar + 2;          // [2]
   uint64_t* drain_bar = tempty_bar + 2;          // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* bfull_bar = drain_bar + 1;           // [1] resident B landed (B-stationary)
+  uint64_t* bempty_bar = bfull_bar + 1;          // [1] every MMA reading the resident B completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bempty_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Two accumulators (power of two, >= 32); NVFP4 adds 32 scale columns per stage after them.
+  // TMEM: two accumulators (columns [0, 2 kBN)); NVFP4 adds its scale columns after
+  // them: streaming 32 per stage (A 16, B 16); B-stationary the resident B scales
+  // (4 per 64-element K chunk) and 16 A columns per stage.
   constexpr int kTmemCols = kFp4 ? 512 : 2 * kBN;
-  static_assert(!kFp4 || 2 * kBN + 32 * kStages <= 512, "TMEM columns");
+  constexpr int kSfbResCols = kStat ? (2 * kBStatK / 64) * 4 : 0;
+  static_assert(!kFp4 || 2 * kBN + kSfbResCols + (kStat ? 16 : 32) * kStages <= 512, "TMEM columns");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -584,6 +709,8 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
       mbar_init(&tempty_bar[a], kEpiWarps);      // one arrive per epilogue warp
     }
     mbar_init(drain_bar, 1);
+    mbar_init(bfull_bar, 1);
+    mbar_init(bempty_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tm_a);
@@ -600,12 +727,12 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
-  const int total_tiles = p.m_tiles * p.n_tiles;
+  const S sched(p);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // The whole warp runs the loop (waits converged); lane 0 issues the copies.
+    {
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed_phase[kStages];
@@ -613,94 +740,160 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
 #pragma unroll
       for (int s = 0; s < kStages; ++s) armed[s] = false, armed_phase[s] = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / p.n_tiles) * kBM;
-        const int nt = tile % p.n_tiles;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
-          uint8_t* sa = smem + L::ab(stage);
-          uint8_t* sb = sa + L::kABytes;
-          if constexpr (kFp4) {
-            // scale chunks of this stage (K = 256 -> up to four 512-byte chunks per operand)
-            const int nch = min(4, p.k_chunks - 4 * kb);
-            const uint32_t sf_bytes = static_cast<uint32_t>(nch) * kSfChunk;
-            mbar_expect_tx(&full_bar[stage], L::kABytes + L::kBBytes + 2 * sf_bytes);
-            const int64_t a_off = (static_cast<int64_t>(m0 / kBM) * p.k_chunks + 4 * kb) * kSfChunk;
-            const int64_t b_off = (static_cast<int64_t>(nt) * p.k_chunks + 4 * kb) * kSfChunk;
-            bulk_load(smem + L::sf(stage), p.sfa + a_off, sf_bytes, &full_bar[stage]);
-            bulk_load(smem + L::sf(stage) + kSfOperandBytes, p.sfb + b_off, sf_bytes, &full_bar[stage]);
-          } else {
-            mbar_expect_tx(&full_bar[stage], L::kStageBytes);
+      int cur_nt = -1;
+      uint32_t nloads = 0;                       // resident-B loads issued
+      for (int t = sched.begin; t < sched.end && ok; t += sched.step) {
+        int mt, nt;
+        S::coords(p, t, mt, nt);
+        const int m0 = mt * kBM;
+        if constexpr (kStat) {
+          if (nt != cur_nt) {
+            // reload the resident B tile once every MMA reading the previous one completed
+            if (nloads > 0 && !wait_warp(bempty_bar, (nloads - 1) & 1u, abort_flag)) { ok = false; break; }
+            uint32_t bytes = static_cast<uint32_t>(p.k_blocks) * L::kBBytes;
+            if constexpr (kFp4) bytes += static_cast<uint32_t>(p.k_chunks) * kSfChunk;
+            if (lane == 0) mbar_expect_tx(bfull_bar, bytes);
+            for (int kb = 0; kb < p.k_blocks && lane == 0; ++kb) {
+              uint8_t* dst = smem + L::kBResOffset + kb * L::kBBytes;
+              if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
+                tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * (kBN / 2));
+                tma_load_2d(dst + (kBN / 2) * kBK, &tm_b2, bfull_bar, kb * kBK, nt * (kBN / 2));
+              } else {
+                tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * kBN);
+              }
+            }
+            if constexpr (kFp4)
+              if (lane == 0)
+                bulk_load(smem + L::kSfbResOffset, p.sfb + static_cast<int64_t>(nt) * p.k_chunks * kSfChunk,
+                          static_cast<uint32_t>(p.k_chunks) * kSfChunk, bfull_bar);
+            __syncwarp();
+            cur_nt = nt;
+            ++nloads;
           }
+        }
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_warp(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           armed[stage] = true;
           armed_phase[stage] = phase;
-          tma_load_2d(sa, &tm_a, &full_bar[stage], kb * kBK, m0);
-          if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
-            tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * (kBN / 2));
-            tma_load_2d(sb + (kBN / 2) * kBK, &tm_b2, &full_bar[stage], kb * kBK, nt * (kBN / 2));
-          } else {
-            tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * kBN);
+          if (lane == 0) {
+            uint8_t* sa = smem + L::a(stage);
+            uint32_t bytes = L::kABytes + (kStat ? 0 : L::kBBytes);
+            const int nch = kFp4 ? min(4, p.k_chunks - 4 * kb) : 0;   // 64-element scale chunks of this stage
+            if constexpr (kFp4) bytes += static_cast<uint32_t>(nch) * kSfChunk * (kStat ? 1 : 2);
+            mbar_expect_tx(&full_bar[stage], bytes);
+            tma_load_2d(sa, &tm_a, &full_bar[stage], kb * kBK, m0);
+            if constexpr (kFp4) {
+              const int64_t a_off = (static_cast<int64_t>(mt) * p.k_chunks + 4 * kb) * kSfChunk;
+              bulk_load(smem + L::sfa(stage), p.sfa + a_off, static_cast<uint32_t>(nch) * kSfChunk, &full_bar[stage]);
+            }
+            if constexpr (!kStat) {
+              uint8_t* sb = smem + L::b(stage);
+              if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
+                tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * (kBN / 2));
+                tma_load_2d(sb + (kBN / 2) * kBK, &tm_b2, &full_bar[stage], kb * kBK, nt * (kBN / 2));
+              } else {
+                tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * kBN);
+              }
+              if constexpr (kFp4) {
+                const int64_t b_off = (static_cast<int64_t>(nt) * p.k_chunks + 4 * kb) * kSfChunk;
+                bulk_load(smem + L::sfb(stage), p.sfb + b_off, static_cast<uint32_t>(nch) * kSfChunk, &full_bar[stage]);
+              }
+            }
           }
+          __syncwarp();
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
       }
-      // Drain: every armed stage's last load has landed before the CTA exits.
+      // Drain: every armed stage's last load (and the last resident B) has landed before the CTA exits.
       for (int s = 0; s < kStages; ++s)
-        if (armed[s]) wait_bounded(&full_bar[s], armed_phase[s], abort_flag);
+        if (armed[s]) wait_warp(&full_bar[s], armed_phase[s], abort_flag);
+      if (kStat && nloads > 0) wait_warp(bfull_bar, (nloads - 1) & 1u, abort_flag);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop (waits converged); lane 0 issues tcgen05 ops.
+    {
       const uint32_t idesc = instr_desc<kAB, kBN>();
+      const uint32_t sfb_res_t = tmem_base + static_cast<uint32_t>(2 * kBN);   // B-stationary NVFP4
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       bool issued = false;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
-        if (!wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) break;
+      int cur_nt = -1;
+      uint32_t bphase = 0;
+      for (int t = sched.begin; t < sched.end && ok; t += sched.step) {
+        int mt, nt;
+        S::coords(p, t, mt, nt);
+        (void)mt;
+        if constexpr (kStat) {
+          if (nt != cur_nt) {
+            if (cur_nt >= 0 && lane == 0) mma_commit(bempty_bar);   // arrives when every MMA on the old B completed
+            __syncwarp();
+            if (!wait_warp(bfull_bar, bphase, abort_flag)) break;
+            bphase ^= 1u;
+            tc_fence_after();
+            if constexpr (kFp4) {
+              if (lane == 0) {
+                const uint32_t src = smem_u32(smem + L::kSfbResOffset);
+                for (int c = 0; c < p.k_chunks; ++c) tmem_cp_sf(sfb_res_t + 4 * c, smem_desc_sf(src + c * kSfChunk));
+              }
+              __syncwarp();
+            }
+            cur_nt = nt;
+          }
+        }
+        if (!wait_warp(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!wait_bounded(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          if (!wait_warp(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + L::ab(stage));
-          const uint32_t b_addr = a_addr + L::kABytes;
-          if constexpr (kFp4) {
-            // Scales -> TMEM (A at columns +0..15, B at +16..31 of this stage's slot),
-            // then one K = 64 MMA per chunk; tcgen05.cp and tcgen05.mma issued by one
-            // thread execute in order.
-            const int nch = min(4, p.k_chunks - 4 * kb);
-            const uint32_t sf_t = tmem_base + static_cast<uint32_t>(2 * kBN + 32 * stage);
-            const uint32_t sf_s = smem_u32(smem + L::sf(stage));
-            for (int c = 0; c < nch; ++c) {
-              tmem_cp_sf(sf_t + 4 * c, smem_desc_sf(sf_s + c * kSfChunk));
-              tmem_cp_sf(sf_t + 16 + 4 * c, smem_desc_sf(sf_s + kSfOperandBytes + c * kSfChunk));
-            }
-            for (int kk = 0; kk < nch; ++kk) {
-              mma_fp4(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
-                      sf_t + 4 * kk, sf_t + 16 + 4 * kk, (kb | kk) != 0);
-            }
-          } else {
+          if (lane == 0) {
+            const uint32_t a_addr = smem_u32(smem + L::a(stage));
+            const uint32_t b_addr =
+                kStat ? smem_u32(smem + L::kBResOffset + kb * L::kBBytes) : smem_u32(smem + L::b(stage));
+            if constexpr (kFp4) {
+              // Scales -> TMEM, then one K = 64 MMA per chunk; tcgen05.cp and
+              // tcgen05.mma issued by one thread execute in order.
+              const int nch = min(4, p.k_chunks - 4 * kb);
+              const uint32_t sfa_t =
+                  tmem_base + static_cast<uint32_t>(2 * kBN + kSfbResCols + (kStat ? 16 : 32) * stage);
+              const uint32_t sf_s = smem_u32(smem + L::sfa(stage));
+              for (int c = 0; c < nch; ++c) {
+                tmem_cp_sf(sfa_t + 4 * c, smem_desc_sf(sf_s + c * kSfChunk));
+                if constexpr (!kStat)
+                  tmem_cp_sf(sfa_t + 16 + 4 * c, smem_desc_sf(smem_u32(smem + L::sfb(stage)) + c * kSfChunk));
+              }
+              for (int kk = 0; kk < nch; ++kk) {
+                const uint32_t sfb_t = kStat ? sfb_res_t + 4 * (4 * kb + kk) : sfa_t + 16 + 4 * kk;
+                mma_fp4(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
+                        sfa_t + 4 * kk, sfb_t, (kb | kk) != 0);
+              }
+            } else {
 #pragma unroll
-            for (int kk = 0; kk < kBK / 32; ++kk) {
-              mma_issue<kInt8>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
-                               (kb | kk) != 0);
+              for (int kk = 0; kk < kBK / 32; ++kk) {
+                mma_issue<kInt8>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
+                                 (kb | kk) != 0);
+              }
             }
+            mma_commit(&empty_bar[stage]);
           }
+          __syncwarp();
           issued = true;
-          mma_commit(&empty_bar[stage]);
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        mma_commit(&tfull_bar[acc]);
+        if (lane == 0) mma_commit(&tfull_bar[acc]);
+        __syncwarp();
         if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
       // Drain: all issued MMAs have completed before TMEM is released.
       if (issued) {
-        mma_commit(drain_bar);
-        wait_bounded(drain_bar, 0, abort_flag);
+        if (lane == 0) mma_commit(drain_bar);
+        __syncwarp();
+        wait_warp(drain_bar, 0, abort_flag);
       }
     }
   } else {
@@ -708,70 +901,147 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     const int ew = warp - kEpiWarp0;             // 0 .. kEpiWarps-1
     const int et = threadIdx.x - kEpiWarp0 * 32; // 0 .. kEpiThreads-1
     const int quarter = warp & 3;                // TMEM lane quarter this warp may access
-    const int half = ew / 4;                     // which share of the columns (8-warp epilogue)
-    const int row_in_tile = quarter * 32 + lane;
-    uint8_t* stage_base = staging + ew * (kStagingBufs * 32 * 128);
-    int sbuf = 0;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    constexpr int kOutCols = (kEpi == EPI_SCALE) ? kBN : kBN / 2;
-    constexpr int kChunkCols = 128 / (kOut == OUT_F32 ? 4 : (kOut == OUT_E4M3 ? 1 : 2));
-    constexpr int kGroupsPerChunk = kChunkCols / 32;
-    constexpr int kGroups = kOutCols / 32 / R::kHalves;   // 32-column groups this warp handles
-    static_assert(kOut == OUT_NVFP4 || kGroups % kGroupsPerChunk == 0, "a warp's columns must be whole store boxes");
-    constexpr bool kParams = !(kFp4 && kEpi != EPI_SCALE);   // NVFP4 SwiGLU takes scalar dequant factors
-    const int g0 = half * kGroups;
-    constexpr int kWordsPerGroup = 32 / kGroupsPerChunk;
-    TileParams<kEpi, kBN, R::kEpiThreads> tp;
-    if (kParams && blockIdx.x < total_tiles) tp.fetch(p, (blockIdx.x % p.n_tiles) * kOutCols, et);
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x) {
-      const int m0 = (tile / p.n_tiles) * kBM;
-      const int n0 = (tile % p.n_tiles) * kOutCols;
-      // Per-column parameters of this tile -> shared memory (zero past column N),
-      // then start fetching the next tile's.
-      if constexpr (kParams) {
+    if constexpr (kOut == OUT_NVFP4) {
+      // 16 warps: TMEM lane quarter x 16-column block of the tile's 64 outputs;
+      // each thread quantizes one NVFP4 block (16 outputs) of its row per tile.
+      static_assert(kOut != OUT_NVFP4 || kEpiWarps == 16, "NVFP4 epilogue layout");
+      const int blk = ew >> 2;
+      const float ag_half = 0.5f * p.a_scale;
+      const float six_gq = __fmul_rn(6.f, p.q_scale);
+      const float r6 = __frcp_rn(six_gq);
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = sched.begin; t < sched.end; t += sched.step) {
+        int mt, nt;
+        S::coords(p, t, mt, nt);
+        const int m = mt * kBM + quarter * 32 + lane;
+        const int n = nt * (kBN / 2) + 16 * blk;    // first output column of this block
+        if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+        uint32_t ga[16], ua[16];
+        tmem_ld16(t_row + 16 * blk, ga);               // gate columns of this block
+        tmem_ld16(t_row + kBN / 2 + 16 * blk, ua);     // up columns
+        tmem_ld_wait(ga, ua);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        uint32_t sc;
+        const uint2 q = swiglu_nvfp4_block(ga, ua, ag_half, p.alpha_up, p.q_scale, six_gq, r6, sc);
+        if (m < p.M) {
+          *reinterpret_cast<uint2*>(p.q_codes + static_cast<int64_t>(m) * (p.N / 2) + n / 2) = q;
+          p.q_sf[(static_cast<int64_t>(m >> 7) * (p.N / 64) + (n >> 6)) * kSfChunk + (m & 31) * 16 +
+                 ((m >> 5) & 3) * 4 + ((n >> 4) & 3)] = static_cast<uint8_t>(sc);
+        }
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    } else {
+      const int half = ew / 4;                     // which share of the columns (8-warp epilogue)
+      const int row_in_tile = quarter * 32 + lane;
+      uint8_t* stage_base = staging + ew * (kStagingBufs * 32 * 128);
+      int sbuf = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      constexpr int kOutCols = (kEpi == EPI_SCALE) ? kBN : kBN / 2;
+      constexpr int kChunkCols = 128 / (kOut == OUT_F32 ? 4 : (kOut == OUT_E4M3 ? 1 : 2));
+      constexpr int kGroupsPerChunk = kChunkCols / 32;
+      constexpr int kGroups = kOutCols / 32 / R::kHalves;   // 32-column groups this warp handles
+      static_assert(kGroups % kGroupsPerChunk == 0, "a warp's columns must be whole store boxes");
+      const int g0 = half * kGroups;
+      constexpr int kWordsPerGroup = 32 / kGroupsPerChunk;
+      TileParams<kEpi, kBN, R::kEpiThreads> tp;
+      if (sched.begin < sched.end) {
+        int mt, nt;
+        S::coords(p, sched.begin, mt, nt);
+        tp.fetch(p, nt * kOutCols, et);
+      }
+      for (int t = sched.begin; t < sched.end; t += sched.step) {
+        int mt, nt;
+        S::coords(p, t, mt, nt);
+        const int m0 = mt * kBM;
+        const int n0 = nt * kOutCols;
+        // Per-column parameters of this tile -> shared memory (zero past column N),
+        // then start fetching the next tile's.
         epilogue_sync<R::kEpiThreads>();
         tp.store(params, et);
         epilogue_sync<R::kEpiThreads>();
-        const int next = tile + gridDim.x;
-        if (next < total_tiles) tp.fetch(p, (next % p.n_tiles) * kOutCols, et);
-      }
-      if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
-      tc_fence_after();
-      const int m = m0 + row_in_tile;
-      const bool row_ok = m < p.M;
-      float sa = p.a_scale;
-      if (p.a_scale_rows != nullptr && row_ok) sa = __ldg(p.a_scale_rows + m);
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
-
-      uint32_t ca[32], cb[32];
-      tmem_load_group<kEpi, kBN>(t_row, g0, ca, cb);
-      uint32_t w[32];
-#pragma unroll
-      for (int g = 0; g < kGroups; ++g) {
-        if constexpr (kEpi == EPI_SCALE) tmem_ld_wait(ca);
-        else tmem_ld_wait(ca, cb);
-        uint32_t na[32], nb[32];
-        if (g + 1 < kGroups) {
-          tmem_load_group<kEpi, kBN>(t_row, g0 + g + 1, na, nb);    // overlaps this group's math
-        } else {
-          // every column of the accumulator is in registers: hand it back to the MMA warp
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        if (t + sched.step < sched.end) {
+          int mt2, nt2;
+          S::coords(p, t + sched.step, mt2, nt2);
+          tp.fetch(p, nt2 * kOutCols, et);
         }
-        const int col = (g0 + g) * 32;           // first output column of this group, tile-relative
-        const int n = n0 + col;
-        if constexpr (kOut == OUT_NVFP4) {
-          // codes [M, N/2]; scales in the tensor-core layout of an [M, N] operand
-          uint4 q;
-          const uint32_t sf2 =
-              swiglu_nvfp4_group(ca, cb, p.a_scale, p.alpha_up, p.q_scale, __fmul_rn(6.f, p.q_scale), q);
-          if (row_ok) {
-            *reinterpret_cast<uint4*>(p.q_codes + static_cast<int64_t>(m) * (p.N / 2) + n / 2) = q;
-            const int64_t sf_off = (static_cast<int64_t>(m >> 7) * (p.N / 64) + (n >> 6)) * kSfChunk +
-                                   (m & 31) * 16 + ((m >> 5) & 3) * 4 + ((n >> 4) & 3);
-            *reinterpret_cast<uint16_t*>(p.q_sf + sf_off) = static_cast<uint16_t>(sf2);
+        if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
+        tc_fence_after();
+        const int m = m0 + row_in_tile;
+        const bool row_ok = m < p.M;
+        float sa = p.a_scale;
+        if (p.a_scale_rows != nullptr && row_ok) sa = __ldg(p.a_scale_rows + m);
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+
+        // Groups stream with a one-group TMEM prefetch; the accumulator goes back to
+        // the MMA warp as soon as its last group is in registers.
+        uint32_t ca[32], cb[32];
+        tmem_load_group<kEpi, kBN>(t_row, g0, ca, cb);
+        uint32_t w[32];
+#pragma unroll
+        for (int g = 0; g < kGroups; ++g) {
+          if constexpr (kEpi == EPI_SCALE) tmem_ld_wait(ca);
+          else tmem_ld_wait(ca, cb);
+          uint32_t na[32], nb[32];
+          if (g + 1 < kGroups) {
+            tmem_load_group<kEpi, kBN>(t_row, g0 + g + 1, na, nb);    // overlaps this group's math
+          } else {
+            // every column of the accumulator is in registers: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+          }
+          const int col = (g0 + g) * 32;           // first output column of this group, tile-relative
+          const int n = n0 + col;
+          float v[32];
+          if constexpr (kEpi == EPI_SCALE) {
+            if (p.a_scale_rows != nullptr) scale_group<kInt8, true>(ca, sa, params + col, params + 256 + col, v);
+            else scale_group<kInt8, false>(ca, sa, params + col, params + 256 + col, v);
+            if (p.residual != nullptr && row_ok) add_residual(p, m, n, v);
+            if (p.out2 != nullptr && row_ok) store_dual_e4m3(p, m, n, v);
+            if constexpr (kOut == OUT_E4M3) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(v[j], p.out_inv);
+            }
+          } else {
+            swiglu_group<kEpi, kOut>(ca, cb, params, g0 + g, p.out_inv, p.out_scale, v);
+          }
+          const int wo = (g % kGroupsPerChunk) * kWordsPerGroup;
+          if constexpr (kOut == OUT_F32) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[wo + j] = __float_as_uint(v[j]);
+          } else if constexpr (kOut == OUT_BF16) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w[wo + j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+          } else if constexpr (kOut == OUT_F16) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w[wo + j] = pack_f16(v[2 * j], v[2 * j + 1]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) w[wo + j] = pack_e4m3x4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          }
+          if (g % kGroupsPerChunk == kGroupsPerChunk - 1) {
+            // ---- stage + TMA store of the 32-row x 128-byte box
+            const int c0 = col - (kGroupsPerChunk - 1) * 32;
+            uint8_t* st = stage_base + sbuf * (32 * 128);
+            if (lane == 0) {                       // the store that last used this buffer has read it
+              if constexpr (kStagingBufs == 2) bulk_wait_read_le1();
+              else bulk_wait_read_all();
+            }
+            __syncwarp();
+            stage_row(st, lane, w);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && m0 + quarter * 32 < p.M) {   // boxes wholly below row M are skipped
+              tma_store_2d(&tm_out, st, n0 + c0, m0 + quarter * 32);
+              bulk_commit();
+            }
+            if constexpr (kStagingBufs == 2) sbuf ^= 1;
           }
           if (g + 1 < kGroups) {
 #pragma unroll
@@ -780,65 +1050,12 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
               cb[j] = nb[j];
             }
           }
-          continue;
         }
-        float v[32];
-        if constexpr (kEpi == EPI_SCALE) {
-          if (p.a_scale_rows != nullptr) scale_group<kInt8, true>(ca, sa, params + col, params + 256 + col, v);
-          else scale_group<kInt8, false>(ca, sa, params + col, params + 256 + col, v);
-          if (p.residual != nullptr && row_ok) add_residual(p, m, n, v);
-          if (p.out2 != nullptr && row_ok) store_dual_e4m3(p, m, n, v);
-          if constexpr (kOut == OUT_E4M3) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(v[j], p.out_inv);
-          }
-        } else {
-          swiglu_group<kEpi, kOut>(ca, cb, params, g0 + g, p.out_inv, p.out_scale, v);
-        }
-        const int wo = (g % kGroupsPerChunk) * kWordsPerGroup;
-        if constexpr (kOut == OUT_F32) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) w[wo + j] = __float_as_uint(v[j]);
-        } else if constexpr (kOut == OUT_BF16) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) w[wo + j] = pack_bf16(v[2 * j], v[2 * j + 1]);
-        } else if constexpr (kOut == OUT_F16) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) w[wo + j] = pack_f16(v[2 * j], v[2 * j + 1]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) w[wo + j] = pack_e4m3x4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        }
-        if (g % kGroupsPerChunk == kGroupsPerChunk - 1) {
-          // ---- stage + TMA store of the 32-row x 128-byte box
-          const int c0 = col - (kGroupsPerChunk - 1) * 32;
-          uint8_t* st = stage_base + sbuf * (32 * 128);
-          if (lane == 0) {                       // the store that last used this buffer has read it
-            if constexpr (kStagingBufs == 2) bulk_wait_read_le1();
-            else bulk_wait_read_all();
-          }
-          __syncwarp();
-          stage_row(st, lane, w);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && m0 + quarter * 32 < p.M) {   // boxes wholly below row M are skipped
-            tma_store_2d(&tm_out, st, n0 + c0, m0 + quarter * 32);
-            bulk_commit();
-          }
-          if constexpr (kStagingBufs == 2) sbuf ^= 1;
-        }
-        if (g + 1 < kGroups) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            ca[j] = na[j];
-            cb[j] = nb[j];
-          }
-        }
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
-      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      if (lane == 0) bulk_wait_all();
+      __syncwarp();
     }
-    if (lane == 0) bulk_wait_all();
-    __syncwarp();
   }
 
   tc_fence_before();

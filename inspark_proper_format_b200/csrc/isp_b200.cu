@@ -2,6 +2,7 @@
 // header is included here so the device error word is shared).
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -104,12 +105,29 @@ constexpr int kSwigluEpiWarps = 4;                         // SwiGLU: 128 output
 #endif
 constexpr int kFp4BN = 128;
 constexpr int kFp4Stages = ISP_GEMM_FP4_STAGES;
+constexpr int kFp4SwigluEpiWarps = 16;   // one NVFP4 block (16 outputs) per thread per tile
 
-template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut>
+// B-stationary schedule (K bytes <= kStatK): the whole B tile stays in shared
+// memory and only A streams, a third of the operand traffic of a 128 x 256 FP8
+// tile (the streaming schedule is bound by L2 -> SM bandwidth).
+constexpr int kStatK = 512;
+constexpr int kStatStages = 4;         // FP8 / INT8: 4 x 16 KB of A + 128 KB of B
+constexpr int kFp4StatStages = 6;      // NVFP4: 6 x 18 KB of A (+ scales) + 72 KB of B (+ scales)
+
+// ISP_GEMM_STREAMING=1 in the environment keeps the streaming schedule (comparisons).
+bool streaming_forced() {
+  static const bool forced = [] {
+    const char* v = getenv("ISP_GEMM_STREAMING");
+    return v != nullptr && v[0] == '1';
+  }();
+  return forced;
+}
+
+template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut, int kBStatK = 0>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, const CUtensorMap& o,
            const Params& p, cudaStream_t stream) {
-  auto kern = gemm_kernel<kBN, kStages, kEpiWarps, kAB, kEpi, kOut>;
-  constexpr int kSmem = Smem<kBN, kStages, kEpiWarps, kAB == AB_FP4 ? kSfStageBytes : 0>::kBytes;
+  auto kern = gemm_kernel<kBN, kStages, kEpiWarps, kAB, kEpi, kOut, kBStatK>;
+  constexpr int kSmem = Smem<kBN, kStages, kEpiWarps, kAB == AB_FP4, kOut != OUT_NVFP4, kBStatK>::kBytes;
   static_assert(kSmem <= 232448, "shared memory budget of one sm_100 CTA");
   static bool configured[64] = {false};
   int dev = 0;
@@ -125,24 +143,28 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, co
   return launch_status();
 }
 
-template <int kAB>
-int dispatch_scale_out(int out_kind, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
-                       const Params& p, cudaStream_t s) {
-  switch (out_kind) {
-    case OUT_BF16: return launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, OUT_BF16>(a, b, b, o, p, s);
-    case OUT_F16: return launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, OUT_F16>(a, b, b, o, p, s);
-    case OUT_F32: return launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, OUT_F32>(a, b, b, o, p, s);
-    case OUT_E4M3: return launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, OUT_E4M3>(a, b, b, o, p, s);
-    default: return ISP_ERR_DTYPE;
+template <int kAB, int kOut>
+int launch_scale(bool stat, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const Params& p,
+                 cudaStream_t s) {
+  if constexpr (kAB == AB_FP4) {
+    return stat ? launch<kFp4BN, kFp4StatStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut, kStatK>(a, b, b, o, p, s)
+                : launch<kFp4BN, kFp4Stages, kScaleEpiWarps, kAB, EPI_SCALE, kOut>(a, b, b, o, p, s);
+  } else {
+    return stat ? launch<kBN, kStatStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut, kStatK>(a, b, b, o, p, s)
+                : launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut>(a, b, b, o, p, s);
   }
 }
 
-int dispatch_fp4_scale_out(int out_kind, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
-                           const Params& p, cudaStream_t s) {
+template <int kAB>
+int dispatch_scale_out(int out_kind, bool stat, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
+                       const Params& p, cudaStream_t s) {
   switch (out_kind) {
-    case OUT_BF16: return launch<kFp4BN, kFp4Stages, kScaleEpiWarps, AB_FP4, EPI_SCALE, OUT_BF16>(a, b, b, o, p, s);
-    case OUT_F16: return launch<kFp4BN, kFp4Stages, kScaleEpiWarps, AB_FP4, EPI_SCALE, OUT_F16>(a, b, b, o, p, s);
-    case OUT_F32: return launch<kFp4BN, kFp4Stages, kScaleEpiWarps, AB_FP4, EPI_SCALE, OUT_F32>(a, b, b, o, p, s);
+    case OUT_BF16: return launch_scale<kAB, OUT_BF16>(stat, a, b, o, p, s);
+    case OUT_F16: return launch_scale<kAB, OUT_F16>(stat, a, b, o, p, s);
+    case OUT_F32: return launch_scale<kAB, OUT_F32>(stat, a, b, o, p, s);
+    case OUT_E4M3:
+      if constexpr (kAB == AB_FP4) return ISP_ERR_DTYPE;
+      else return launch_scale<kAB, OUT_E4M3>(stat, a, b, o, p, s);
     default: return ISP_ERR_DTYPE;
   }
 }
@@ -326,8 +348,9 @@ int isp_scaled_gemm(const void* A, const void* W, int ab_dtype, int64_t M, int N
   p.out_inv = out_inv_scale;
   p.out2 = out2;
   p.out2_inv = out2_inv_scale;
-  return ab_dtype == ISP_I8 ? dispatch_scale_out<AB_I8>(out_kind, ta, tb, to, p, stream)
-                            : dispatch_scale_out<AB_E4M3>(out_kind, ta, tb, to, p, stream);
+  const bool stat = K <= kStatK && !streaming_forced();
+  return ab_dtype == ISP_I8 ? dispatch_scale_out<AB_I8>(out_kind, stat, ta, tb, to, p, stream)
+                            : dispatch_scale_out<AB_E4M3>(out_kind, stat, ta, tb, to, p, stream);
 }
 
 int isp_gated_up(const void* A, const void* W1, const void* W3, int interleaved, int64_t M, int N, int K,
@@ -368,13 +391,20 @@ int isp_gated_up(const void* A, const void* W1, const void* W3, int interleaved,
   p.w_scale2 = s3;
   p.out_inv = static_cast<float>(1.0 / static_cast<double>(out_scale));
   p.out_scale = out_scale;
+  const bool stat = K <= kStatK && !streaming_forced();
+  constexpr int kSt = kStatStages + 1;   // 4 epilogue warps leave room for a fifth A stage
   if (interleaved) {
-    return out_kind == OUT_E4M3
-               ? launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_INTERLEAVED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
-               : launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_INTERLEAVED, OUT_F32>(ta, tb, tb2, to, p, stream);
+    if (out_kind == OUT_E4M3)
+      return stat ? launch<kBN, kSt, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_INTERLEAVED, OUT_E4M3, kStatK>(ta, tb, tb2, to, p, stream)
+                  : launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_INTERLEAVED, OUT_E4M3>(ta, tb, tb2, to, p, stream);
+    return stat ? launch<kBN, kSt, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_INTERLEAVED, OUT_F32, kStatK>(ta, tb, tb2, to, p, stream)
+                : launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_INTERLEAVED, OUT_F32>(ta, tb, tb2, to, p, stream);
   }
-  return out_kind == OUT_E4M3 ? launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_E4M3>(ta, tb, tb2, to, p, stream)
-                              : launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_F32>(ta, tb, tb2, to, p, stream);
+  if (out_kind == OUT_E4M3)
+    return stat ? launch<kBN, kSt, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_E4M3, kStatK>(ta, tb, tb2, to, p, stream)
+                : launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_E4M3>(ta, tb, tb2, to, p, stream);
+  return stat ? launch<kBN, kSt, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_F32, kStatK>(ta, tb, tb2, to, p, stream)
+              : launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_F32>(ta, tb, tb2, to, p, stream);
 }
 
 int isp_nvfp4_scales_to_mma(const void* src, int64_t R, int K, void* dst, isp_stream_t stream) {
@@ -425,7 +455,8 @@ int isp_nvfp4_gemm(const void* A, const void* A_sf, const void* W, const void* W
   p.bias = bias;
   p.residual = residual;
   p.residual_f32 = residual_dtype == ISP_F32;
-  return dispatch_fp4_scale_out(out_kind, ta, tb, to, p, stream);
+  const bool stat = K / 2 <= kStatK && !streaming_forced();
+  return dispatch_scale_out<AB_FP4>(out_kind, stat, ta, tb, to, p, stream);
 }
 
 int isp_nvfp4_gated_up(const void* A, const void* A_sf, const void* W13, const void* W13_sf, int64_t M, int N, int K,
@@ -462,7 +493,11 @@ int isp_nvfp4_gated_up(const void* A, const void* A_sf, const void* W13, const v
   p.q_codes = static_cast<uint8_t*>(h_codes);
   p.q_sf = static_cast<uint8_t*>(h_sf);
   // The output map is unused by the NVFP4 epilogue (direct stores); pass A's.
-  return launch<kFp4BN, kFp4Stages, kScaleEpiWarps, AB_FP4, EPI_SWIGLU_PAIRED, OUT_NVFP4>(ta, tb, tb, ta, p, stream);
+  if (K / 2 <= kStatK && !streaming_forced())
+    return launch<kFp4BN, kFp4StatStages + 2, kFp4SwigluEpiWarps, AB_FP4, EPI_SWIGLU_PAIRED, OUT_NVFP4, kStatK>(
+        ta, tb, tb, ta, p, stream);
+  return launch<kFp4BN, kFp4Stages, kFp4SwigluEpiWarps, AB_FP4, EPI_SWIGLU_PAIRED, OUT_NVFP4>(ta, tb, tb, ta, p,
+                                                                                          stream);
 }
 
 }  // extern "C"
