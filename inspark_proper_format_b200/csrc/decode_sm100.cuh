@@ -1,0 +1,264 @@
+// Small-M (decode) W8A8 GEMM: out[M <= 128, N] = epilogue(A . W^T), K split
+// across a thread-block cluster, partial sums reduced through distributed
+// shared memory.  Decode is bound by streaming the weight once from HBM; with
+// one 128 x 256 tile per CTA the regular kernel would run only N/256 CTAs, each
+// reading a whole K row block of W and all of A.  Here a cluster of S CTAs
+// shares one 128-column N tile:
+//   * CTA r of the cluster runs the TMA -> tcgen05 main loop over K blocks
+//     [r kb/S, (r+1) kb/S) into one TMEM accumulator (128 lanes x 128 columns),
+//     then writes its partial (rows < M) to its own shared memory;
+//   * after a cluster barrier, CTA r sums the S partials of its 128/S output
+//     columns (peer shared memory via ld.shared::cluster, fixed order q = 0..S-1)
+//     and applies the epilogue of the regular kernel (scale, bias, residual);
+//   * a second cluster barrier keeps every CTA's shared memory alive until all
+//     readers are done.
+// No global workspace, one launch.  Every CTA reaches both cluster barriers on
+// every path (including expired waits), so a peer can never be left waiting.
+// INT8 partial sums are int32 and add exactly; FP8 partial sums are FP32 and
+// add in the fixed rank order (deterministic, rounding order differs from the
+// single-CTA kernel by the split).
+#pragma once
+
+#include "gemm_sm100.cuh"
+
+namespace isp {
+namespace gemm {
+
+constexpr int kDecBN = 128;
+constexpr int kDecStages = 4;
+constexpr int kDecThreads = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 TMEM -> shared
+constexpr int kDecRowStride = 528;        // bytes per partial row: 128 x 4 B + 16 B (conflict-free 16-byte stores)
+
+struct DecSmem {
+  static constexpr int kABytes = kBM * kBK;        // 16 KB
+  static constexpr int kBBytes = kDecBN * kBK;     // 16 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kRedOffset = kDecStages * kStageBytes;
+  static constexpr int kRedBytes = kBM * kDecRowStride;
+  static constexpr int kBarOffset = kRedOffset + kRedBytes;
+  static constexpr int kBytes = kBarOffset + 128;
+};
+
+ISP_D uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster arrives (release) and waits (acquire).
+ISP_D void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+ISP_D uint32_t map_to_rank(uint32_t local_smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
+  return r;
+}
+ISP_D uint4 ld_cluster_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+template <bool kInt8>
+ISP_D float dec_acc(uint32_t bits) {
+  if constexpr (kInt8) return static_cast<float>(static_cast<int32_t>(bits));
+  else return __uint_as_float(bits);
+}
+
+// The regular kernel's EPI_SCALE arithmetic for one value (see scale_group).
+template <bool kInt8>
+ISP_D float dec_scale(float acc, const Params& p, float sa, int n) {
+  const float ws = p.w_scale != nullptr ? __ldg(p.w_scale + n) : 1.f;
+  const float b = p.bias != nullptr ? __ldg(p.bias + n) : 0.f;
+  if (p.a_scale_rows != nullptr) {
+    if constexpr (kInt8) return __fadd_rn(__fmul_rn(acc, __fmul_rn(sa, ws)), b);
+    else return __fmaf_rn(__fmul_rn(acc, sa), ws, b);
+  }
+  const float c = __fmul_rn(p.a_scale, ws);
+  if constexpr (kInt8) return __fadd_rn(__fmul_rn(acc, c), b);
+  else return __fmaf_rn(acc, c, b);
+}
+
+template <bool kInt8, int kOut>
+__global__ void __launch_bounds__(kDecThreads, 1)
+    decode_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, const Params p,
+                  int splits) {
+  using L = DecSmem;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  // A misaligned base skips the work but still takes part in both cluster barriers.
+  const bool aligned = (smem_u32(smem) & 1023u) == 0;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty_bar = full_bar + kDecStages;
+  uint64_t* tfull_bar = empty_bar + kDecStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* red = smem + L::kRedOffset;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rank = static_cast<int>(cluster_rank());
+  const int n0 = blockIdx.y * kDecBN;
+  const int kb0 = static_cast<int>(static_cast<int64_t>(rank) * p.k_blocks / splits);
+  const int kb1 = static_cast<int>(static_cast<int64_t>(rank + 1) * p.k_blocks / splits);
+
+  if (threadIdx.x == 0) {
+    if (!aligned) atomicExch(&g_device_error, (int)ISP_ERR_ALIGN);
+    for (int s = 0; s < kDecStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(tfull_bar, 1);
+    *abort_flag = aligned ? 0 : 1;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&tm_a);
+    prefetch_tmap(&tm_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kDecBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const bool run = aligned;
+
+  if (warp == 0 && run) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool armed[kDecStages] = {false, false, false, false};
+    uint32_t armed_phase[kDecStages] = {0, 0, 0, 0};
+    for (int kb = kb0; kb < kb1; ++kb) {
+      if (!wait_warp(&empty_bar[stage], phase ^ 1u, abort_flag)) break;
+      armed[stage] = true;
+      armed_phase[stage] = phase;
+      if (lane == 0) {
+        uint8_t* sa = smem + stage * L::kStageBytes;
+        mbar_expect_tx(&full_bar[stage], L::kStageBytes);
+        tma_load_2d(sa, &tm_a, &full_bar[stage], kb * kBK, 0);
+        tma_load_2d(sa + L::kABytes, &tm_b, &full_bar[stage], kb * kBK, n0);
+      }
+      __syncwarp();
+      if (++stage == kDecStages) { stage = 0; phase ^= 1u; }
+    }
+    for (int s = 0; s < kDecStages; ++s)
+      if (armed[s]) wait_warp(&full_bar[s], armed_phase[s], abort_flag);
+  } else if (warp == 1 && run) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idesc = instr_desc<kInt8 ? AB_I8 : AB_E4M3, kDecBN>();
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int kb = kb0; kb < kb1; ++kb) {
+      if (!wait_warp(&full_bar[stage], phase, abort_flag)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+        const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 32; ++kk)
+          mma_issue<kInt8>(tmem_base, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
+                           (kb > kb0 || kk > 0) ? 1u : 0u);
+        mma_commit(&empty_bar[stage]);
+      }
+      __syncwarp();
+      if (++stage == kDecStages) { stage = 0; phase ^= 1u; }
+    }
+    if (lane == 0) mma_commit(tfull_bar);    // also the drain: arrives once every issued MMA completed
+    __syncwarp();
+    wait_warp(tfull_bar, 0, abort_flag);
+  } else if (warp >= 2 && run) {
+    // ------------------------------------------------ TMEM -> shared partial
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const bool have = kb1 > kb0;
+    if (wait_bounded(tfull_bar, 0, abort_flag)) {
+      tc_fence_after();
+      uint8_t* dst = red + row * kDecRowStride;
+#pragma unroll
+      for (int g = 0; g < kDecBN / 32; ++g) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + g * 32, r);
+        tmem_ld_wait(r);
+        if (row < p.M) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint4 v = have ? make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]) : make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(dst + (g * 32 + 4 * j) * 4) = v;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();    // every partial of the cluster is in shared memory
+
+  // ------------------------------------------- cluster reduction + epilogue
+  if (run) {
+    const int cols = kDecBN / splits;          // this CTA's output columns
+    const int c0 = rank * cols;
+    const int vec_per_row = cols / 4;
+    const int items = p.M * vec_per_row;
+    for (int i = threadIdx.x; i < items; i += kDecThreads) {
+      const int m = i / vec_per_row;
+      const int c = c0 + 4 * (i - m * vec_per_row);
+      const int n = n0 + c;
+      if (n >= p.N) continue;                  // N % 16 == 0: a 4-column group is wholly in or out
+      const uint32_t local = smem_u32(red + m * kDecRowStride + c * 4);
+      float v[4];
+      if constexpr (kInt8) {
+        int32_t s4[4] = {0, 0, 0, 0};
+        for (int q = 0; q < splits; ++q) {
+          const uint4 t = ld_cluster_v4(map_to_rank(local, q));
+          s4[0] += static_cast<int32_t>(t.x); s4[1] += static_cast<int32_t>(t.y);
+          s4[2] += static_cast<int32_t>(t.z); s4[3] += static_cast<int32_t>(t.w);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = static_cast<float>(s4[j]);
+      } else {
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int q = 0; q < splits; ++q) {
+          const uint4 t = ld_cluster_v4(map_to_rank(local, q));
+          s4[0] = __fadd_rn(s4[0], __uint_as_float(t.x)); s4[1] = __fadd_rn(s4[1], __uint_as_float(t.y));
+          s4[2] = __fadd_rn(s4[2], __uint_as_float(t.z)); s4[3] = __fadd_rn(s4[3], __uint_as_float(t.w));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = s4[j];
+      }
+      const float sa = p.a_scale_rows != nullptr ? __ldg(p.a_scale_rows + m) : p.a_scale;
+      const int64_t off = static_cast<int64_t>(m) * p.N + n;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[j] = dec_scale<kInt8>(v[j], p, sa, n + j);
+        if (p.residual != nullptr) {
+          const float r = p.residual_f32 ? __ldg(static_cast<const float*>(p.residual) + off + j)
+                                         : __bfloat162float(static_cast<const __nv_bfloat16*>(p.residual)[off + j]);
+          v[j] = __fadd_rn(v[j], r);
+        }
+      }
+      if constexpr (kOut == OUT_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off) = make_float4(v[0], v[1], v[2], v[3]);
+      } else if constexpr (kOut == OUT_BF16) {
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + off) =
+            make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
+      } else {
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + off) =
+            make_uint2(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]));
+      }
+    }
+  }
+  cluster_sync_all();    // no CTA leaves while a peer may still read its shared memory
+
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kDecBN));
+  }
+}
+
+}  // namespace gemm
+}  // namespace isp

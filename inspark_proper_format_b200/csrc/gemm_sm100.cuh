@@ -74,6 +74,7 @@ struct Params {
   float out_scale;        // SwiGLU dequant multiplier (F32 output)
   void* out2;             // residual-dual E4M3 output
   float out2_inv;
+  void* out;              // output base (direct-store paths; TMA stores use the tensor map)
   // NVFP4 operands: block scales of A and B in the tensor-core layout
   // (chunk (r/128, k/64) of 512 bytes at ((r/128) * k_chunks + k/64) * 512).
   const uint8_t* sfa;

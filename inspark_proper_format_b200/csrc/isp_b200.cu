@@ -8,6 +8,7 @@
 #include "common.cuh"
 #include "fir.cuh"
 #include "gemm_sm100.cuh"
+#include "decode_sm100.cuh"
 #include "norm_quant.cuh"
 
 namespace isp {
@@ -183,6 +184,58 @@ __global__ void scales_to_mma_kernel(const uint32_t* src, int64_t R, int kchunks
   dst[off] = v;
 }
 
+// Small-M path: cluster split-K (decode_sm100.cuh).  ISP_GEMM_NO_DECODE=1 keeps
+// the regular kernel for M <= 128 (comparisons).
+bool decode_disabled() {
+  static const bool off = [] {
+    const char* v = getenv("ISP_GEMM_NO_DECODE");
+    return v != nullptr && v[0] == '1';
+  }();
+  return off;
+}
+
+template <bool kInt8, int kOut>
+int launch_decode(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int splits, int n_tiles,
+                  cudaStream_t stream) {
+  auto kern = decode_kernel<kInt8, kOut>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DecSmem::kBytes) != cudaSuccess)
+      return ISP_ERR_LAUNCH;
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(splits), static_cast<unsigned>(n_tiles), 1);
+  cfg.blockDim = dim3(kDecThreads, 1, 1);
+  cfg.dynamicSmemBytes = DecSmem::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, a, b, p, splits) != cudaSuccess) {
+    cudaGetLastError();
+    return ISP_ERR_LAUNCH;
+  }
+  return launch_status();
+}
+
+template <bool kInt8>
+int dispatch_decode(int out_kind, const CUtensorMap& a, const CUtensorMap& b, const Params& p, int splits,
+                    int n_tiles, cudaStream_t s) {
+  switch (out_kind) {
+    case OUT_BF16: return launch_decode<kInt8, OUT_BF16>(a, b, p, splits, n_tiles, s);
+    case OUT_F16: return launch_decode<kInt8, OUT_F16>(a, b, p, splits, n_tiles, s);
+    case OUT_F32: return launch_decode<kInt8, OUT_F32>(a, b, p, splits, n_tiles, s);
+    default: return ISP_ERR_DTYPE;
+  }
+}
+
 int out_kind_of(int dtype) {
   switch (dtype) {
     case ISP_BF16: return OUT_BF16;
@@ -328,6 +381,30 @@ int isp_scaled_gemm(const void* A, const void* W, int ab_dtype, int64_t M, int N
     return ISP_ERR_ALIGN;
   if (int st = isp::check_device()) return st;
   if (M == 0) return ISP_OK;
+  if (M <= kBM && out2 == nullptr && out_kind != OUT_E4M3 && !decode_disabled()) {
+    // decode: one 128-column N tile per cluster, K split over up to 8 CTAs
+    CUtensorMap ta, tb;
+    if (!make_map(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, kBK, kBM) ||
+        !make_map(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, kBK, kDecBN))
+      return ISP_ERR_ALIGN;
+    Params p{};
+    p.M = static_cast<int>(M);
+    p.N = N;
+    p.K = K;
+    p.k_blocks = (K + kBK - 1) / kBK;
+    p.a_scale = a_scale;
+    p.a_scale_rows = a_scale_rows;
+    p.w_scale = w_scale;
+    p.bias = bias;
+    p.residual = residual;
+    p.residual_f32 = residual_dtype == ISP_F32;
+    p.out = out;
+    const int n_tiles = (N + kDecBN - 1) / kDecBN;
+    int splits = 8;
+    while (splits > 1 && (n_tiles * splits > isp::sm_count() || splits > p.k_blocks)) splits >>= 1;
+    return ab_dtype == ISP_I8 ? dispatch_decode<true>(out_kind, ta, tb, p, splits, n_tiles, stream)
+                              : dispatch_decode<false>(out_kind, ta, tb, p, splits, n_tiles, stream);
+  }
   CUtensorMap ta, tb, to;
   if (!make_map(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, kBK, kBM) ||
       !make_map(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, kBK, kBN) || !make_out_map(&to, out, out_kind, M, N))

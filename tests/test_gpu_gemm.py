@@ -231,3 +231,31 @@ def test_shape_and_dtype_errors(G):
     with pytest.raises(ValueError):
         G.scaled_gemm(torch.zeros(4, 32, device="cuda").to(torch.float8_e4m3fn),
                       torch.zeros(16, 32, device="cuda", dtype=torch.int8))  # mixed operand types
+
+
+@pytest.mark.parametrize("m", [1, 64, 128])
+@pytest.mark.parametrize("n,k", [(1280, 1280), (3840, 1280), (1280, 5120), (5120, 1280), (208, 2048), (128, 128)])
+def test_int8_decode_split_k_bit_exact(G, m, n, k):
+    """M <= 128 runs the cluster split-K kernel: int32 partials add exactly."""
+    g = np.random.default_rng(3 * m + n + k)
+    qa = g.integers(-128, 128, (m, k), dtype=np.int64).astype(np.int8)
+    qw = g.integers(-127, 128, (n, k), dtype=np.int64).astype(np.int8)
+    sa = np.float32(1 / 127)
+    sw = (g.random(n).astype(np.float32) * 1e-3 + 1e-4).astype(np.float32)
+    bias = (g.standard_normal(n) * 0.1).astype(np.float32)
+    r = g.standard_normal((m, n)).astype(np.float32)
+    y = G.i8_residual(torch.from_numpy(qa).cuda(), torch.from_numpy(qw).cuda(), float(sa), torch.from_numpy(sw).cuda(),
+                      torch.from_numpy(bias).cuda(), torch.from_numpy(r).cuda())
+    np.testing.assert_array_equal(y.cpu().numpy(), og.int8_gemm(qa, qw, sa, sw, bias, r))
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 3840, 1280), (17, 1280, 5120), (128, 512, 1536)])
+def test_fp8_decode_row_scales_residual(G, m, n, k):
+    a, w, sa, sw, bias = fp8_operands(m, n, k, 29)
+    rows = (np.random.default_rng(4).random(m).astype(np.float32) + 0.5) * sa
+    res = torch.from_numpy(np.random.default_rng(5).standard_normal((m, n)).astype(np.float32)).bfloat16()
+    y = G.scaled_gemm(dev_codes(a), dev_codes(w), a_scale_rows=torch.from_numpy(rows).cuda(),
+                      w_scale=torch.from_numpy(sw).cuda(), bias=torch.from_numpy(bias).cuda(),
+                      residual=res.cuda(), out_dtype=torch.float16)
+    ref = og.fp8_gemm(a, w, rows, sw, bias, residual=res.float().numpy(), out="f32")
+    assert rel_l2(y.float().cpu().numpy(), ref) < 1e-3      # F16 output rounding
