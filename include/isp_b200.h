@@ -113,6 +113,23 @@ int isp_norm_quant(const void *x, int x_dtype, int64_t M, int K,
                    void *codes, void *scales_out, isp_stream_t stream);
 
 /*
+ * gpt_fast AdaptiveLayerNorm fused with the quantizer:
+ *   y = ada_w[g] * RMSNorm_gptfast(x) + ada_b[g],   g = row / rows_per_group,
+ * multiply and add as separate FP32 roundings, then quantized as isp_norm_quant.
+ *
+ * Replaces: AdaptiveLayerNorm.forward  models/indextts2/upstream/s2mel/modules/gpt_fast/model.py:18-32
+ *   (the DiT's attention/FFN norms) followed by its Q/DQ.
+ *
+ * ada_w, ada_b: [M / rows_per_group, K] FP32 (the split projection of each
+ * utterance's conditioning embedding), 16-byte aligned; M % rows_per_group == 0.
+ * Other arguments as isp_norm_quant with norm_kind ISP_NORM_RMS_GPTFAST.
+ */
+int isp_adaln_quant(const void *x, int x_dtype, int64_t M, int K, const float *gamma, float eps,
+                    const float *ada_w, const float *ada_b, int64_t rows_per_group, int qfmt,
+                    float scale, const float *smooth, void *codes, void *scales_out,
+                    isp_stream_t stream);
+
+/*
  * Reorders E4M3 block scales [R, K/16] (row-major, the ModelOpt storage order
  * of scripts/export_nvfp4_weights.py:38) into the tensor-core layout described
  * at ISP_Q_NVFP4_MMA.  dst must hold ceil(R/128)*128*K/16 bytes; padding rows

@@ -306,9 +306,34 @@ int isp_norm_quant(const void* x, int x_dtype, int64_t M, int K, const float* ga
   if (qfmt == ISP_Q_NVFP4 && (reinterpret_cast<uintptr_t>(scales_out) & 1)) return ISP_ERR_ALIGN;
   if (int st = isp::check_device()) return st;
   if (M == 0) return ISP_OK;
-  isp::NormQuantParams p{x, M, K, gamma, bias, eps, out_mul, scale, smooth, codes, scales_out};
+  isp::NormQuantParams p{x, M, K, gamma, bias, eps, out_mul, scale, smooth, codes, scales_out, nullptr, nullptr, 1};
   return x_dtype == ISP_BF16 ? isp::launch_norm_quant_kind<true>(norm_kind, qfmt, p, stream)
                              : isp::launch_norm_quant_kind<false>(norm_kind, qfmt, p, stream);
+}
+
+int isp_adaln_quant(const void* x, int x_dtype, int64_t M, int K, const float* gamma, float eps, const float* ada_w,
+                    const float* ada_b, int64_t rows_per_group, int qfmt, float scale, const float* smooth,
+                    void* codes, void* scales_out, isp_stream_t stream) {
+  if (ada_w == nullptr || ada_b == nullptr || gamma == nullptr) return ISP_ERR_ARG;
+  if (rows_per_group <= 0 || M % rows_per_group != 0) return ISP_ERR_SHAPE;
+  if (!isp::aligned16(ada_w) || !isp::aligned16(ada_b)) return ISP_ERR_ALIGN;
+  // shared validation of the plain entry (norm kind fixed to gpt_fast RMSNorm)
+  if (x == nullptr || codes == nullptr) return ISP_ERR_ARG;
+  if (x_dtype != ISP_BF16 && x_dtype != ISP_F32) return ISP_ERR_DTYPE;
+  if (M < 0 || K <= 0 || K % 16 != 0) return ISP_ERR_SHAPE;
+  if (qfmt < ISP_Q_E4M3_STATIC || qfmt > ISP_Q_NVFP4_MMA) return ISP_ERR_ARG;
+  const bool nvfp4 = qfmt == ISP_Q_NVFP4 || qfmt == ISP_Q_NVFP4_MMA;
+  if (qfmt == ISP_Q_NVFP4_MMA && K % 64 != 0) return ISP_ERR_SHAPE;
+  if ((qfmt == ISP_Q_E4M3_ROW || nvfp4) && scales_out == nullptr) return ISP_ERR_ARG;
+  if (qfmt != ISP_Q_E4M3_ROW && !isp::gemm::global_scale_ok(scale)) return ISP_ERR_ARG;
+  if (!isp::aligned16(x) || !isp::aligned16(codes) || !isp::aligned16(gamma) || (smooth && !isp::aligned16(smooth)))
+    return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  if (M == 0) return ISP_OK;
+  isp::NormQuantParams p{x, M, K, gamma, nullptr, eps, 1.f, scale, smooth, codes, scales_out, ada_w, ada_b,
+                         rows_per_group};
+  return x_dtype == ISP_BF16 ? isp::launch_norm_quant_kind<true>(ISP_NORM_RMS_GPTFAST, qfmt, p, stream)
+                             : isp::launch_norm_quant_kind<false>(ISP_NORM_RMS_GPTFAST, qfmt, p, stream);
 }
 
 int isp_fir_snake(const float* x, int64_t rows, int C, int64_t T, const float* up,

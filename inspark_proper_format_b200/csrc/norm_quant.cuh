@@ -24,6 +24,10 @@ struct NormQuantParams {
   const float* smooth;  // INT8 SmoothQuant divisor or nullptr
   void* codes;
   void* scales_out;
+  // AdaLN (RMS_GPTFAST only): y = ada_w[g] * norm(x) + ada_b[g], g = row / rows_per_group
+  const float* ada_w;
+  const float* ada_b;
+  int64_t rows_per_group;
 };
 
 ISP_D void load_param8(const float* base, int g, float (&w)[8]) {
@@ -108,12 +112,19 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
       if (g < ngroups) {
         float gm[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
         if constexpr (kNorm == ISP_NORM_RMS_GPTFAST || kNorm == ISP_NORM_RMS_QWEN) load_param8(p.gamma, g, gm);
+        float aw[8], ab[8];
+        if (kNorm == ISP_NORM_RMS_GPTFAST && p.ada_w != nullptr) {
+          const int64_t grp = row / p.rows_per_group;
+          load_param8(p.ada_w + grp * K, g, aw);
+          load_param8(p.ada_b + grp * K, g, ab);
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           float y = __fmul_rn(v[i][j], r);
           if constexpr (kNorm == ISP_NORM_RMS_GPTFAST) {
             if constexpr (kBF16) y = bf16_round(y);
             y = __fmul_rn(y, gm[j]);
+            if (p.ada_w != nullptr) y = __fadd_rn(__fmul_rn(aw[j], y), ab[j]);
           } else if constexpr (kNorm == ISP_NORM_RMS_QWEN) {
             y = __fmul_rn(y, gm[j]);
             if constexpr (kBF16) y = bf16_round(y);

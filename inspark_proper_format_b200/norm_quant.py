@@ -104,3 +104,61 @@ def quantize_fp8(x: torch.Tensor, input_scale: float) -> torch.Tensor:
     view packs four codes per word (``codes.view(torch.int32)``)."""
     codes, _ = norm_quant(x, kind="none", fmt="e4m3", scale=input_scale)
     return codes
+
+
+def adaln_quant(x: torch.Tensor, gamma: torch.Tensor, ada_w: torch.Tensor, ada_b: torch.Tensor, *,
+                fmt: str = "e4m3", eps: float = 1e-6, scale: float | None = None,
+                global_scale: float | None = None, smooth: torch.Tensor | None = None):
+    """gpt_fast ``AdaptiveLayerNorm`` fused with the quantizer
+    (``gpt_fast/model.py:18-32``): ``ada_w[b] * RMSNorm(x) + ada_b[b]`` for
+    ``x`` [B, T, K] (or [B*T, K] with ``ada_w`` [B, K]), then ``fmt`` as in
+    ``norm_quant``.  ``ada_w``/``ada_b`` are the split projection of each
+    utterance's conditioning embedding, FP32 [B, K]."""
+    if fmt not in FORMATS:
+        raise ValueError(f"unknown format {fmt!r}")
+    if x.dtype not in (torch.bfloat16, torch.float32) or not x.is_cuda:
+        raise ValueError("adaln_quant expects a CUDA BF16 or FP32 tensor")
+    x = x.contiguous()
+    k = x.shape[-1]
+    m = x.numel() // k if k else 0
+    ada_w = ada_w.float().reshape(-1, k).contiguous()
+    ada_b = ada_b.float().reshape(-1, k).contiguous()
+    groups = ada_w.shape[0]
+    if ada_b.shape[0] != groups or groups == 0 or m % groups:
+        raise ValueError("ada_w/ada_b must hold one [K] row per utterance and divide the rows evenly")
+    gamma = _param(gamma, k, "gamma")
+    smooth = _param(smooth, k, "smooth")
+    lead = x.shape[:-1]
+    scales = None
+    if fmt in ("nvfp4", "nvfp4_mma"):
+        if global_scale is None:
+            raise ValueError("nvfp4 needs the FP32 global scale")
+        s = float(global_scale)
+        codes = torch.empty(*lead, k // 2, device=x.device, dtype=torch.uint8)
+        scales = (torch.empty(*lead, k // 16, device=x.device, dtype=torch.float8_e4m3fn) if fmt == "nvfp4"
+                  else torch.zeros(mma_scale_bytes(m, k), device=x.device, dtype=torch.uint8))
+    else:
+        s = float(scale) if fmt in ("e4m3", "int8") else 0.0
+        if fmt in ("e4m3", "int8") and scale is None:
+            raise ValueError(f"{fmt} needs a calibrated static scale")
+        codes = torch.empty(*lead, k, device=x.device, dtype=torch.int8 if fmt == "int8" else torch.float8_e4m3fn)
+        if fmt == "e4m3_row":
+            scales = torch.empty(*lead, device=x.device, dtype=torch.float32)
+    status = _lib.load().isp_adaln_quant(
+        x.data_ptr(), _lib.BF16 if x.dtype == torch.bfloat16 else _lib.F32, m, k, gamma.data_ptr(), float(eps),
+        ada_w.data_ptr(), ada_b.data_ptr(), m // groups, FORMATS[fmt], s, _lib.ptr(smooth), codes.data_ptr(),
+        _lib.ptr(scales), _lib.stream_handle(x.device))
+    _lib.check(status, "isp_adaln_quant")
+    return codes, scales
+
+
+def adaptive_layer_norm_quant(module, x: torch.Tensor, embedding: torch.Tensor, **quant):
+    """Drop-in for ``AdaptiveLayerNorm(x, embedding)`` followed by its Q/DQ: the
+    module's own ``project_layer`` turns the [B, 1, K] embedding into the
+    per-utterance (weight, bias); its ``norm`` supplies gamma and eps."""
+    if embedding is None:
+        return norm_quant(x, kind="rms_gptfast", gamma=module.norm.weight.detach().float(), eps=module.eps, **quant)
+    with torch.no_grad():
+        w, b = torch.split(module.project_layer(embedding).float(), module.d_model, dim=-1)
+    return adaln_quant(x, module.norm.weight.detach().float().contiguous(), w.reshape(-1, module.d_model),
+                       b.reshape(-1, module.d_model), eps=module.eps, **quant)

@@ -47,6 +47,21 @@ def rms_norm_gptfast(x: np.ndarray, gamma: np.ndarray, eps: float, input_is_bf16
     return (y * np.asarray(gamma, np.float32)).astype(np.float32)
 
 
+def adaptive_layer_norm(x: np.ndarray, gamma: np.ndarray, eps: float, ada_w: np.ndarray, ada_b: np.ndarray,
+                        rows_per_group: int, input_is_bf16: bool) -> np.ndarray:
+    """gpt_fast ``AdaptiveLayerNorm.forward`` with its RMSNorm
+    (``models/indextts2/upstream/s2mel/modules/gpt_fast/model.py:18-32``):
+    ``weight * norm(x) + bias`` where (weight, bias) are the FP32 projection of
+    the conditioning embedding, one [K] pair per utterance.  Rows are grouped
+    ``rows_per_group`` per utterance (the [B, T, K] -> [B*T, K] flattening);
+    the multiply and the add are separate FP32 roundings."""
+    y = rms_norm_gptfast(x, gamma, eps, input_is_bf16)
+    g = np.arange(y.shape[0]) // int(rows_per_group)
+    w = np.asarray(ada_w, np.float32)[g]
+    b = np.asarray(ada_b, np.float32)[g]
+    return ((w * y).astype(np.float32) + b).astype(np.float32)
+
+
 def rms_norm_qwen(x: np.ndarray, gamma: np.ndarray, eps: float, input_is_bf16: bool) -> np.ndarray:
     """Qwen-style ``RMSNorm.forward`` (``models/indextts2/dspark/draft.py:19-23``).
 

@@ -87,6 +87,24 @@ def main(reference_root: str):
                          eps=np.float32(1e-6), scale=np.float32(scale), y_bf16=_bf16_bits(y), qdq=qdq.numpy(),
                          codes=_fp8_codes(codes)))
 
+    # --- gpt_fast AdaptiveLayerNorm (RMSNorm + per-utterance FP32 affine) + _QDQ -------
+    from inspark_infer.models.indextts2.upstream.s2mel.modules.gpt_fast.model import AdaptiveLayerNorm
+    ada = AdaptiveLayerNorm(512, RMSNorm(512, eps=1e-6))
+    with torch.no_grad():
+        ada.norm.weight.copy_(norm.weight)
+        ga = torch.Generator().manual_seed(7)
+        ada.project_layer.weight.copy_(torch.randn(1024, 512, generator=ga) * 0.02)
+        ada.project_layer.bias.copy_(torch.randn(1024, generator=ga) * 0.1
+                                     + torch.cat([torch.ones(512), torch.zeros(512)]))
+        emb = torch.randn(4, 1, 512, generator=ga)             # 4 utterances x 64 frames
+        y = ada(x.view(4, 64, 512), emb).reshape(256, 512)     # FP32
+        w, b = torch.split(ada.project_layer(emb), 512, dim=-1)
+        scale = torch.tensor(float(y.abs().amax()) / 448.0)
+        codes = (y / scale).clamp(-448, 448).to(torch.float8_e4m3fn)
+    written.append(_save("normquant_adaln_e4m3", x_bf16=_bf16_bits(x), gamma=ada.norm.weight.detach().numpy(),
+                         eps=np.float32(1e-6), ada_w=w.reshape(4, 512).numpy(), ada_b=b.reshape(4, 512).numpy(),
+                         rows_per_group=np.int64(64), scale=np.float32(scale), y=y.numpy(), codes=_fp8_codes(codes)))
+
     # --- Zipformer BiasNorm (FP32) + ZipVoice export_qdq ------------------------------
     xf = activations(192, 512, 5, 10.0, 2)
     bn = BiasNorm(512)

@@ -124,3 +124,40 @@ def test_errors_are_reported_before_launch(nq):
         nq(x, kind="none", fmt="e4m3", scale=1.0)          # K % 16 != 0
     with pytest.raises(ValueError):
         nq(torch.randn(4, 32, device="cuda").bfloat16(), kind="rms_gptfast", fmt="e4m3", scale=1.0)  # no gamma
+
+
+def test_golden_adaptive_layer_norm(nq):
+    """AdaLN (gpt_fast AdaptiveLayerNorm) fused with static E4M3, against the reference fixture."""
+    from inspark_proper_format_b200.norm_quant import adaln_quant
+    d = np.load(GOLDEN / "normquant_adaln_e4m3.npz")
+    x = torch.from_numpy(bits_to_bf16(d["x_bf16"])).bfloat16()
+    codes, _ = adaln_quant(x.cuda(), torch.from_numpy(d["gamma"]).cuda(), torch.from_numpy(d["ada_w"]).cuda(),
+                           torch.from_numpy(d["ada_b"]).cuda(), eps=float(d["eps"]), scale=float(d["scale"]))
+    got = codes.view(torch.uint8).cpu().numpy()
+    assert np.mean(got != d["codes"]) < 1e-4      # reference FP32 row-sum order, documented
+    ref = onq.quant_e4m3_static(onq.adaptive_layer_norm(bits_to_bf16(d["x_bf16"]), d["gamma"], float(d["eps"]),
+                                                        d["ada_w"], d["ada_b"], int(d["rows_per_group"]), True),
+                                float(d["scale"]))
+    np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "nvfp4"])
+@pytest.mark.parametrize("b,t,k", [(3, 50, 512), (2, 7, 1280)])
+def test_adaln_bit_exact(nq, fmt, b, t, k):
+    from inspark_proper_format_b200.norm_quant import adaln_quant
+    g = torch.Generator().manual_seed(b * t + k)
+    x = torch.randn(b * t, k, generator=g).bfloat16()
+    gamma = torch.rand(k, generator=g) * 0.2 + 0.9
+    w = torch.randn(b, k, generator=g) * 0.1 + 1.0
+    bb = torch.randn(b, k, generator=g) * 0.1
+    y = onq.adaptive_layer_norm(x.float().numpy(), gamma.numpy(), 1e-6, w.numpy(), bb.numpy(), t, True)
+    if fmt == "e4m3":
+        scale = float(np.abs(y).max() / 448)
+        codes, _ = adaln_quant(x.cuda(), gamma.cuda(), w.cuda(), bb.cuda(), scale=scale)
+        np.testing.assert_array_equal(codes.view(torch.uint8).cpu().numpy(), onq.quant_e4m3_static(y, scale))
+    else:
+        gs = float(np.float32(np.abs(y).max() / (6 * 448)))
+        codes, sf = adaln_quant(x.cuda(), gamma.cuda(), w.cuda(), bb.cuda(), fmt="nvfp4", global_scale=gs)
+        rp, rs = onq.quant_nvfp4(y, gs)
+        np.testing.assert_array_equal(codes.cpu().numpy(), rp)
+        np.testing.assert_array_equal(sf.view(torch.uint8).cpu().numpy(), rs)

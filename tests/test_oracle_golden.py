@@ -49,6 +49,17 @@ def test_gptfast_rmsnorm_then_static_e4m3():
     np.testing.assert_array_equal((e4m3_decode(exact) * d["scale"]).astype(np.float32), d["qdq"])
 
 
+def test_adaptive_layer_norm_then_static_e4m3():
+    d = load("normquant_adaln_e4m3")
+    x = bits_to_bf16(d["x_bf16"])
+    y = normquant.adaptive_layer_norm(x, d["gamma"], float(d["eps"]), d["ada_w"], d["ada_b"],
+                                      int(d["rows_per_group"]), True)
+    assert np.mean(y != d["y"]) < 1e-4           # rare rows: torch's FP32 running row sum
+    np.testing.assert_allclose(y, d["y"], rtol=1e-5, atol=1e-6)
+    exact = normquant.quant_e4m3_static(d["y"], float(d["scale"]))
+    np.testing.assert_array_equal(exact, d["codes"])
+
+
 def test_qwen_rmsnorm_then_static_e4m3():
     d = load("normquant_qwen_e4m3")
     x = bits_to_bf16(d["x_bf16"])
