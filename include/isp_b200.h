@@ -138,6 +138,68 @@ int isp_adaln_quant(const void *x, int x_dtype, int64_t M, int K, const float *g
 int isp_nvfp4_scales_to_mma(const void *src, int64_t R, int K, void *dst, isp_stream_t stream);
 
 /*
+ * Quantized learned convolutions (groups 1, zero padding) as a polyphase
+ * implicit GEMM on tcgen05.  A Conv1d (stride S) is one phase whose K blocks
+ * are (tap, 128 channels) boxes of channels-last codes; a ConvTranspose1d
+ * (stride S) is S phases, phase r producing output times q * S + r from the
+ * taps with tap * dilation = r + padding (mod S) -- the same products as the
+ * reference's zero-insertion rewrite and its gather kernel, without the
+ * (S - 1) / S zero rows.  Three calls: pack the weight once, quantize the
+ * input, run the convolution.
+ *
+ * Replaces: ops/triton/fp8_conv.py:24-62 (conv1d, the FP8 MatrixConv path of
+ *   ops/matrix.py:21-31 with weights from quantization/precision.py:15-56) and
+ *   ExportWeightOp.forward for conv roles (build/unified_acoustic_export.py:
+ *   156-216, static FP8 / INT8 SmoothQuant Q/DQ, zero-insertion rewrite).
+ */
+
+/* Phase count and taps per phase of a convolution geometry (for sizing the
+ * packed weight [phases, CO, taps, C_pad]).  phases * taps <= 128. */
+int isp_conv1d_geometry(int KW, int stride, int dilation, int padding, int transposed,
+                        int *phases, int *taps);
+
+/*
+ * Weight codes [CI * KW, ldw] (E4M3 or INT8 bytes; row ci * KW + tap, column
+ * co: the packed [K, N] layout of quantization/weights.py:5-17, whose per-
+ * output-channel scales are used unchanged; for ConvTranspose1d the rows come
+ * from weight.permute(1, 0, 2) as in quantization/precision.py:34-36) ->
+ * w_packed [phases, CO, taps, C_pad], zero past CI and in empty tap slots.
+ * ldw >= CO; C_pad % 128 == 0, C_pad >= CI; w_packed 16-byte aligned.
+ */
+int isp_conv1d_pack_weight(const void *codes, int64_t ldw, int CO, int CI, int KW, int stride,
+                           int dilation, int padding, int transposed, void *w_packed, int C_pad,
+                           isp_stream_t stream);
+
+/*
+ * Input quantization: x [B, C, T] (x_dtype ISP_F32 or ISP_BF16, channels first)
+ * -> channels-last codes xq [B, T_rows, C_pad], T_rows = T rounded up to a
+ * multiple of row_multiple (the Conv1d stride; 1 for ConvTranspose1d), rows >= T
+ * and channels >= C coded 0.
+ *   static scale (amax == NULL, in_scale > 0): E4M3 e4m3(clamp(x / in_scale)),
+ *     INT8 rne(x / smooth[c] / in_scale) saturated (smooth may be NULL);
+ *   dynamic per-utterance scale (amax != NULL, in_scale == 0, E4M3 only): the
+ *     call writes amax[b] = max |x[b]| and codes x / max(amax[b] / 448, 1e-12)
+ *     (ops/triton/fp8_conv.py:6-22); pass the same amax to isp_conv1d.
+ */
+int isp_conv1d_quant(const void *x, int x_dtype, int64_t B, int C, int64_t T, int row_multiple,
+                     const float *smooth, float in_scale, float *amax, int code_dtype, void *xq,
+                     int C_pad, isp_stream_t stream);
+
+/*
+ * y[b, co, t] = acc * s_in * w_scale[co] + bias[co] with acc the exact-product,
+ * FP32-accumulated sum over (tap, ci) of xq codes times weight codes, s_in =
+ * in_scale (static) or max(amax[b] / 448, 1e-12) (dynamic).  T_out must equal
+ * (T_in + 2 padding - dilation (KW - 1) - 1) / stride + 1 (Conv1d) or
+ * (T_in - 1) stride - 2 padding + dilation (KW - 1) + output_padding + 1
+ * (ConvTranspose1d).  xq from isp_conv1d_quant with the same geometry; ab_dtype
+ * ISP_E4M3 or ISP_I8; y [B, CO, T_out] in ISP_F32, ISP_BF16 or ISP_F16.
+ */
+int isp_conv1d(const void *xq, int ab_dtype, int64_t B, int C_pad, int64_t T_in, const void *w_packed,
+               int CO, int KW, int stride, int dilation, int padding, int output_padding,
+               int transposed, int64_t T_out, float in_scale, const float *amax,
+               const float *w_scale, const float *bias, void *y, int out_dtype, isp_stream_t stream);
+
+/*
  * BigVGAN anti-aliased Snake activation: 2x 12-tap polyphase upsample with
  * replicate padding, Snake v + inv_beta[c] * sin(alpha[c] v)^2, 12-tap
  * stride-2 replicate-padded low-pass, fused in one pass over x.

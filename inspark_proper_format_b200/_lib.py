@@ -28,6 +28,11 @@ SIGNATURES = {
     "isp_read_device_error": (_i, [ctypes.POINTER(_i), _i, _vp]),
     "isp_norm_quant": (_i, [_vp, _i, _i64, _i, _vp, _vp, _f, _f, _i, _i, _f, _vp, _vp, _vp, _vp]),
     "isp_adaln_quant": (_i, [_vp, _i, _i64, _i, _vp, _f, _vp, _vp, _i64, _i, _f, _vp, _vp, _vp, _vp]),
+    "isp_conv1d_geometry": (_i, [_i, _i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "isp_conv1d_pack_weight": (_i, [_vp, _i64, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _vp]),
+    "isp_conv1d_quant": (_i, [_vp, _i, _i64, _i, _i64, _i, _vp, _f, _vp, _i, _vp, _i, _vp]),
+    "isp_conv1d": (_i, [_vp, _i, _i64, _i, _i64, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _f, _vp, _vp, _vp, _vp,
+                        _i, _vp]),
     "isp_fir_snake": (_i, [_vp, _i64, _i, _i64, _vp, _vp, _vp, _vp, _vp, _i, _vp, _f, _vp]),
     "isp_scaled_gemm": (_i, [_vp, _vp, _i, _i64, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _vp, _i, _f, _vp, _f, _vp]),
     "isp_gated_up": (_i, [_vp, _vp, _vp, _i, _i64, _i, _i, _vp, _vp, _f, _vp, _i, _vp]),

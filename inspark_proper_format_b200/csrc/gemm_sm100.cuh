@@ -50,7 +50,10 @@ struct Roles {
 };
 
 enum AbKind { AB_E4M3 = 0, AB_I8 = 1, AB_FP4 = 2 };
-enum EpiKind { EPI_SCALE = 0, EPI_SWIGLU_PAIRED = 1, EPI_SWIGLU_INTERLEAVED = 2 };
+// EPI_CONV: the scale epilogue of a polyphase implicit-GEMM convolution (A rows =
+// output times of one phase of one utterance, A gathered per (tap, 128-channel)
+// block from channels-last codes; output stored transposed to [B, CO, T_out]).
+enum EpiKind { EPI_SCALE = 0, EPI_SWIGLU_PAIRED = 1, EPI_SWIGLU_INTERLEAVED = 2, EPI_CONV = 3 };
 // OUT_NVFP4: packed E2M1 codes + E4M3 block scales in the tensor-core layout.
 enum OutKind { OUT_BF16 = 0, OUT_F16 = 1, OUT_F32 = 2, OUT_E4M3 = 3, OUT_NVFP4 = 4 };
 
@@ -59,6 +62,10 @@ ISP_HD int out_bytes(int out) { return out == OUT_F32 ? 4 : ((out == OUT_E4M3 ||
 constexpr int kSfChunk = 512;                        // 128 rows x 4 E4M3 scales (K = 64)
 constexpr int kSfOperandBytes = 4 * kSfChunk;        // one operand's scales for a 256-element K stage
 constexpr int kSfStageBytes = 2 * kSfOperandBytes;   // A and B scales of one stage
+constexpr int kConvTab = 128;                        // (phase, tap) entries of an implicit conv
+
+// Dynamic per-utterance input scale of the FP8 implicit conv: max(amax / 448, 1e-12).
+ISP_D float conv_dynamic_scale(float amax) { return fmaxf(__fdiv_rn(amax, 448.f), 1e-12f); }
 
 struct Params {
   int M, N, K;            // N = logical output columns
@@ -84,6 +91,20 @@ struct Params {
   float q_scale;          // NVFP4 output: global scale of h
   uint8_t* q_codes;       // NVFP4 output: packed E2M1 [M, N/2]
   uint8_t* q_sf;          // NVFP4 output: block scales, tensor-core layout
+  // EPI_CONV (polyphase implicit-GEMM Conv1d / ConvTranspose1d):
+  //   m tile mt -> utterance mt / conv_tpb, first phase row q0 = (mt % conv_tpb) * 128;
+  //   n tile nt -> phase r = nt / conv_ntco, output channels (nt % conv_ntco) * kBN;
+  //   K block kb -> table entry e = conv_tab[r * conv_taps + kb / conv_cblocks]: the A box
+  //   starts at row q0 + (e >> 10) and 128-byte column ((e & 1023) + kb % conv_cblocks);
+  //   phase row q of phase r is output time q * conv_phases + r.
+  int conv_tpb;
+  int conv_ntco;
+  int conv_phases;
+  int conv_taps;
+  int conv_cblocks;
+  int64_t conv_tout;
+  const float* conv_amax; // per-utterance |x| max (dynamic input scale) or nullptr
+  int conv_tab[kConvTab];
 };
 
 // Shared-memory layout.  Streaming (kBStatK == 0): stage s = [A | B | A scales | B scales].
@@ -188,6 +209,13 @@ ISP_D void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, in
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+ISP_D void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 ISP_D void tma_store_2d(const CUtensorMap* map, const void* smem_src, int c0, int c1) {
@@ -405,6 +433,13 @@ ISP_D void lds32(const float* p, float (&v)[32]) {   // uniform address: a broad
 // Columns at or past N read as 0, so the math needs no column guards.
 // For EPI_SCALE with a per-tensor activation scale the staged column scale is
 // already sa * w_scale[n] (the product the INT8 reference forms as AS * WS[n]).
+// First output column of n tile nt (EPI_CONV: tiles of every phase cover the same channels).
+template <int kEpi, int kOutCols>
+ISP_D int tile_col0(const Params& p, int nt) {
+  if constexpr (kEpi == EPI_CONV) return (nt % p.conv_ntco) * kOutCols;
+  return nt * kOutCols;
+}
+
 template <int kEpi, int kBN, int kEpiThreads>
 struct TileParams {
   static constexpr int kPer = 256 / kEpiThreads;
@@ -415,7 +450,7 @@ struct TileParams {
     for (int h = 0; h < kPer; ++h) {
       const int i = et + kEpiThreads * h;
       float x = 0.f, y = 0.f;
-      if constexpr (kEpi == EPI_SCALE) {
+      if constexpr (kEpi == EPI_SCALE || kEpi == EPI_CONV) {
         const int n = n0 + i;
         if (i < kBN && n < p.N) {
           x = p.w_scale != nullptr ? __ldg(p.w_scale + n) : 1.f;
@@ -444,7 +479,7 @@ struct TileParams {
 // Issue the TMEM loads of output group g (32 output columns).
 template <int kEpi, int kBN>
 ISP_D void tmem_load_group(uint32_t t_row, int g, uint32_t (&a)[32], uint32_t (&b)[32]) {
-  if constexpr (kEpi == EPI_SCALE) {
+  if constexpr (kEpi == EPI_SCALE || kEpi == EPI_CONV) {
     tmem_ld32(t_row + g * 32, a);
   } else if constexpr (kEpi == EPI_SWIGLU_PAIRED) {
     tmem_ld32(t_row + g * 32, a);                // gate
@@ -662,7 +697,7 @@ template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut, int 
 __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_out,
-                const Params p) {
+                const __grid_constant__ Params p) {
   constexpr bool kInt8 = kAB == AB_I8;
   constexpr bool kFp4 = kAB == AB_FP4;
   constexpr bool kStat = kBStatK > 0;
@@ -747,6 +782,11 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         int mt, nt;
         S::coords(p, t, mt, nt);
         const int m0 = mt * kBM;
+        int cr = 0, cnt = nt;                    // EPI_CONV: phase and output-channel tile
+        if constexpr (kEpi == EPI_CONV) {
+          cr = nt / p.conv_ntco;
+          cnt = nt - cr * p.conv_ntco;
+        }
         if constexpr (kStat) {
           if (nt != cur_nt) {
             // reload the resident B tile once every MMA reading the previous one completed
@@ -759,6 +799,8 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
               if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
                 tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * (kBN / 2));
                 tma_load_2d(dst + (kBN / 2) * kBK, &tm_b2, bfull_bar, kb * kBK, nt * (kBN / 2));
+              } else if constexpr (kEpi == EPI_CONV) {
+                tma_load_3d(dst, &tm_b, bfull_bar, kb * kBK, cnt * kBN, cr);
               } else {
                 tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * kBN);
               }
@@ -782,7 +824,15 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
             const int nch = kFp4 ? min(4, p.k_chunks - 4 * kb) : 0;   // 64-element scale chunks of this stage
             if constexpr (kFp4) bytes += static_cast<uint32_t>(nch) * kSfChunk * (kStat ? 1 : 2);
             mbar_expect_tx(&full_bar[stage], bytes);
-            tma_load_2d(sa, &tm_a, &full_bar[stage], kb * kBK, m0);
+            if constexpr (kEpi == EPI_CONV) {
+              const int b = mt / p.conv_tpb;
+              const int j = kb / p.conv_cblocks;
+              const int e = p.conv_tab[cr * p.conv_taps + j];
+              const int q0 = (mt - b * p.conv_tpb) * kBM;
+              tma_load_3d(sa, &tm_a, &full_bar[stage], ((e & 1023) + kb - j * p.conv_cblocks) * kBK, q0 + (e >> 10), b);
+            } else {
+              tma_load_2d(sa, &tm_a, &full_bar[stage], kb * kBK, m0);
+            }
             if constexpr (kFp4) {
               const int64_t a_off = (static_cast<int64_t>(mt) * p.k_chunks + 4 * kb) * kSfChunk;
               bulk_load(smem + L::sfa(stage), p.sfa + a_off, static_cast<uint32_t>(nch) * kSfChunk, &full_bar[stage]);
@@ -792,6 +842,8 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
               if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
                 tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * (kBN / 2));
                 tma_load_2d(sb + (kBN / 2) * kBK, &tm_b2, &full_bar[stage], kb * kBK, nt * (kBN / 2));
+              } else if constexpr (kEpi == EPI_CONV) {
+                tma_load_3d(sb, &tm_b, &full_bar[stage], kb * kBK, cnt * kBN, cr);
               } else {
                 tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * kBN);
               }
@@ -943,7 +995,8 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
       int sbuf = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      constexpr int kOutCols = (kEpi == EPI_SCALE) ? kBN : kBN / 2;
+      constexpr bool kScaleLike = kEpi == EPI_SCALE || kEpi == EPI_CONV;
+      constexpr int kOutCols = kScaleLike ? kBN : kBN / 2;
       constexpr int kChunkCols = 128 / (kOut == OUT_F32 ? 4 : (kOut == OUT_E4M3 ? 1 : 2));
       constexpr int kGroupsPerChunk = kChunkCols / 32;
       constexpr int kGroups = kOutCols / 32 / R::kHalves;   // 32-column groups this warp handles
@@ -954,13 +1007,13 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
       if (sched.begin < sched.end) {
         int mt, nt;
         S::coords(p, sched.begin, mt, nt);
-        tp.fetch(p, nt * kOutCols, et);
+        tp.fetch(p, tile_col0<kEpi, kOutCols>(p, nt), et);
       }
       for (int t = sched.begin; t < sched.end; t += sched.step) {
         int mt, nt;
         S::coords(p, t, mt, nt);
         const int m0 = mt * kBM;
-        const int n0 = nt * kOutCols;
+        const int n0 = tile_col0<kEpi, kOutCols>(p, nt);
         // Per-column parameters of this tile -> shared memory (zero past column N),
         // then start fetching the next tile's.
         epilogue_sync<R::kEpiThreads>();
@@ -969,14 +1022,21 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         if (t + sched.step < sched.end) {
           int mt2, nt2;
           S::coords(p, t + sched.step, mt2, nt2);
-          tp.fetch(p, nt2 * kOutCols, et);
+          tp.fetch(p, tile_col0<kEpi, kOutCols>(p, nt2), et);
         }
         if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
         tc_fence_after();
         const int m = m0 + row_in_tile;
-        const bool row_ok = m < p.M;
+        // EPI_CONV: the row is phase row q of phase nt / conv_ntco, output time ct of utterance cu
+        const int cu = kEpi == EPI_CONV ? mt / p.conv_tpb : 0;
+        const int64_t ct = kEpi == EPI_CONV ? (static_cast<int64_t>(mt - cu * p.conv_tpb) * kBM + row_in_tile) *
+                                                      p.conv_phases + nt / p.conv_ntco
+                                            : 0;
+        const bool row_ok = kEpi == EPI_CONV ? ct < p.conv_tout : m < p.M;
         float sa = p.a_scale;
         if (p.a_scale_rows != nullptr && row_ok) sa = __ldg(p.a_scale_rows + m);
+        if constexpr (kEpi == EPI_CONV)
+          if (p.conv_amax != nullptr) sa = conv_dynamic_scale(__ldg(p.conv_amax + cu));
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
 
         // Groups stream with a one-group TMEM prefetch; the accumulator goes back to
@@ -986,7 +1046,7 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         uint32_t w[32];
 #pragma unroll
         for (int g = 0; g < kGroups; ++g) {
-          if constexpr (kEpi == EPI_SCALE) tmem_ld_wait(ca);
+          if constexpr (kScaleLike) tmem_ld_wait(ca);
           else tmem_ld_wait(ca, cb);
           uint32_t na[32], nb[32];
           if (g + 1 < kGroups) {
@@ -1000,6 +1060,30 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
           const int col = (g0 + g) * 32;           // first output column of this group, tile-relative
           const int n = n0 + col;
           float v[32];
+          if constexpr (kEpi == EPI_CONV) {
+            if (p.conv_amax != nullptr) scale_group<kInt8, true>(ca, sa, params + col, params + 256 + col, v);
+            else scale_group<kInt8, false>(ca, sa, params + col, params + 256 + col, v);
+            // transposed direct store to [B, CO, T_out]: for each channel the 32 lanes
+            // write 32 times conv_phases apart (one 128-byte row segment for FP32 and
+            // one phase; the other phases' tiles fill the gaps)
+            if (row_ok) {
+              const int64_t base = static_cast<int64_t>(cu) * p.N * p.conv_tout + ct;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (n + j < p.N) {
+                  const int64_t off = base + static_cast<int64_t>(n + j) * p.conv_tout;
+                  if constexpr (kOut == OUT_F32) static_cast<float*>(p.out)[off] = v[j];
+                  else if constexpr (kOut == OUT_F16) static_cast<__half*>(p.out)[off] = __float2half_rn(v[j]);
+                  else static_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(v[j]);
+                }
+              }
+            }
+            if (g + 1 < kGroups) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) ca[j] = na[j];
+            }
+            continue;
+          }
           if constexpr (kEpi == EPI_SCALE) {
             if (p.a_scale_rows != nullptr) scale_group<kInt8, true>(ca, sa, params + col, params + 256 + col, v);
             else scale_group<kInt8, false>(ca, sa, params + col, params + 256 + col, v);

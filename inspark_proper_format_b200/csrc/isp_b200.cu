@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "conv.cuh"
 #include "fir.cuh"
 #include "gemm_sm100.cuh"
 #include "decode_sm100.cuh"
@@ -75,6 +76,20 @@ bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int el
   cuuint32_t estr[2] = {1, 1};
   return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 3-D row-major uint8 tensor [d2, d1, d0] (d0 innermost) with a (box0 x box1 x 1) box, 128-byte swizzle.
+bool make_map3d_u8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t box0,
+                   uint32_t box1) {
+  EncodeFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0, d0 * d1};
+  cuuint32_t box[3] = {box0, box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -236,6 +251,76 @@ int dispatch_decode(int out_kind, const CUtensorMap& a, const CUtensorMap& b, co
   }
 }
 
+// Polyphase tap table of a convolution.  Conv1d (stride S): one phase; slot j is
+// tap j at input position t * S + o, o = j * dilation - padding, which in the A view
+// [rows / S, S * C_pad] is row t + floor(o / S), column block (o mod S) * C_pad / 128.
+// ConvTranspose1d (stride S): output time t = q * S + r gathers input q + (r + padding
+// - tap * dilation) / S from the taps with tap * dilation = r + padding (mod S); phase
+// r lists those taps (zero slots pad every phase to the same count).
+struct ConvGeom {
+  int phases, taps, a_stride;
+  int tap[kConvTab];
+  int row[kConvTab];
+  int colstep[kConvTab];
+};
+
+inline int64_t floor_div(int64_t a, int64_t b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
+
+int conv_geometry(int KW, int stride, int dilation, int padding, int transposed, ConvGeom* g) {
+  // |row offsets| < 2^19 keeps row * 1024 + column in an int
+  if (KW < 1 || stride < 1 || dilation < 1 || padding < 0 || KW > 4096 || stride > 4096 ||
+      static_cast<int64_t>(dilation) * (KW - 1) + padding >= (1 << 19))
+    return ISP_ERR_SHAPE;
+  if (!transposed) {
+    if (KW > kConvTab) return ISP_ERR_SHAPE;
+    g->phases = 1;
+    g->taps = KW;
+    g->a_stride = stride;
+    for (int j = 0; j < KW; ++j) {
+      const int64_t o = static_cast<int64_t>(j) * dilation - padding;
+      const int64_t row = floor_div(o, stride);
+      g->tap[j] = j;
+      g->row[j] = static_cast<int>(row);
+      g->colstep[j] = static_cast<int>(o - row * stride);
+    }
+    return ISP_OK;
+  }
+  g->phases = stride;
+  g->a_stride = 1;
+  int taps = 1;
+  for (int r = 0; r < stride; ++r) {
+    int n = 0;
+    for (int k = 0; k < KW; ++k)
+      if ((static_cast<int64_t>(r) + padding - static_cast<int64_t>(k) * dilation) % stride == 0) ++n;
+    taps = n > taps ? n : taps;
+  }
+  if (static_cast<int64_t>(stride) * taps > kConvTab) return ISP_ERR_SHAPE;
+  g->taps = taps;
+  for (int r = 0; r < stride; ++r) {
+    int n = 0;
+    for (int k = 0; k < KW; ++k) {
+      const int64_t num = static_cast<int64_t>(r) + padding - static_cast<int64_t>(k) * dilation;
+      if (num % stride != 0) continue;
+      g->tap[r * taps + n] = k;
+      g->row[r * taps + n] = static_cast<int>(floor_div(num, stride));
+      g->colstep[r * taps + n] = 0;
+      ++n;
+    }
+    for (; n < taps; ++n) {
+      g->tap[r * taps + n] = -1;
+      g->row[r * taps + n] = 0;
+      g->colstep[r * taps + n] = 0;
+    }
+  }
+  return ISP_OK;
+}
+
+template <int kAB, int kOut>
+int launch_conv(bool stat, const CUtensorMap& a, const CUtensorMap& b, const Params& p, cudaStream_t s) {
+  return stat ? launch<kBN, kStatStages, kScaleEpiWarps, kAB, EPI_CONV, kOut, kStatK>(a, b, b, a, p, s)
+              : launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_CONV, kOut>(a, b, b, a, p, s);
+}
+
 int out_kind_of(int dtype) {
   switch (dtype) {
     case ISP_BF16: return OUT_BF16;
@@ -334,6 +419,163 @@ int isp_adaln_quant(const void* x, int x_dtype, int64_t M, int K, const float* g
                          rows_per_group};
   return x_dtype == ISP_BF16 ? isp::launch_norm_quant_kind<true>(ISP_NORM_RMS_GPTFAST, qfmt, p, stream)
                              : isp::launch_norm_quant_kind<false>(ISP_NORM_RMS_GPTFAST, qfmt, p, stream);
+}
+
+int isp_conv1d_geometry(int KW, int stride, int dilation, int padding, int transposed, int* phases, int* taps) {
+  isp::gemm::ConvGeom g;
+  if (phases == nullptr || taps == nullptr) return ISP_ERR_ARG;
+  if (int st = isp::gemm::conv_geometry(KW, stride, dilation, padding, transposed, &g)) return st;
+  *phases = g.phases;
+  *taps = g.taps;
+  return ISP_OK;
+}
+
+int isp_conv1d_pack_weight(const void* codes, int64_t ldw, int CO, int CI, int KW, int stride, int dilation,
+                           int padding, int transposed, void* w_packed, int C_pad, isp_stream_t stream) {
+  isp::gemm::ConvGeom g;
+  if (codes == nullptr || w_packed == nullptr) return ISP_ERR_ARG;
+  if (CO <= 0 || CI <= 0 || ldw < CO || C_pad < CI || C_pad % 128 != 0) return ISP_ERR_SHAPE;
+  if (int st = isp::gemm::conv_geometry(KW, stride, dilation, padding, transposed, &g)) return st;
+  if (!isp::aligned16(w_packed)) return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  isp::ConvPackParams p{};
+  p.src = static_cast<const uint8_t*>(codes);
+  p.ldw = ldw;
+  p.CO = CO;
+  p.CI = CI;
+  p.KW = KW;
+  p.phases = g.phases;
+  p.taps = g.taps;
+  p.c_pad = C_pad;
+  p.dst = static_cast<uint8_t*>(w_packed);
+  for (int i = 0; i < g.phases * g.taps; ++i) p.tap[i] = g.tap[i];
+  const int64_t total = static_cast<int64_t>(g.phases) * CO * g.taps * (C_pad / 16);
+  isp::conv_pack_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(p);
+  return isp::launch_status();
+}
+
+int isp_conv1d_quant(const void* x, int x_dtype, int64_t B, int C, int64_t T, int row_multiple, const float* smooth,
+                     float in_scale, float* amax, int code_dtype, void* xq, int C_pad, isp_stream_t stream) {
+  if (x == nullptr || xq == nullptr) return ISP_ERR_ARG;
+  if (x_dtype != ISP_F32 && x_dtype != ISP_BF16) return ISP_ERR_DTYPE;
+  if (code_dtype != ISP_E4M3 && code_dtype != ISP_I8) return ISP_ERR_DTYPE;
+  if (smooth != nullptr && code_dtype != ISP_I8) return ISP_ERR_ARG;
+  if (amax != nullptr && (code_dtype != ISP_E4M3 || in_scale != 0.f)) return ISP_ERR_ARG;
+  if (amax == nullptr && !isp::gemm::global_scale_ok(in_scale)) return ISP_ERR_ARG;
+  if (B < 0 || C <= 0 || T <= 0 || row_multiple < 1 || C_pad < C || C_pad % 128 != 0) return ISP_ERR_SHAPE;
+  if (!isp::aligned16(xq)) return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  if (B == 0) return ISP_OK;
+  if (amax != nullptr) {
+    if (cudaMemsetAsync(amax, 0, static_cast<size_t>(B) * sizeof(float), stream) != cudaSuccess)
+      return ISP_ERR_LAUNCH;
+    const int64_t per = static_cast<int64_t>(C) * T;
+    const int64_t want = (per + 256 * 16 - 1) / (256 * 16);         // >= 16 elements per thread
+    const unsigned bx = static_cast<unsigned>(want < 1024 ? want : 1024);
+    const dim3 grid(bx, static_cast<unsigned>(B));
+    if (B > 65535) return ISP_ERR_SHAPE;
+    if (x_dtype == ISP_BF16) isp::conv_amax_kernel<true><<<grid, 256, 0, stream>>>(x, per, amax);
+    else isp::conv_amax_kernel<false><<<grid, 256, 0, stream>>>(x, per, amax);
+  }
+  isp::ConvQuantParams p{};
+  p.x = x;
+  p.B = B;
+  p.C = C;
+  p.T = T;
+  p.t_rows = (T + row_multiple - 1) / row_multiple * row_multiple;
+  p.c_pad = C_pad;
+  p.chunks = C_pad / 16;
+  // RN(1/s): the host division is IEEE single precision, the reciprocal the kernels expect
+  p.scale = amax != nullptr ? 1.f : in_scale;
+  p.rscale = 1.f / p.scale;
+  p.amax = amax;
+  p.smooth = smooth;
+  p.xq = static_cast<uint8_t*>(xq);
+  const int64_t total = B * p.chunks * p.t_rows;
+  const unsigned grid = static_cast<unsigned>((total + 255) / 256);
+  const bool bf16 = x_dtype == ISP_BF16;
+  if (code_dtype == ISP_I8) {
+    if (bf16) isp::conv_quant_kernel<true, true><<<grid, 256, 0, stream>>>(p);
+    else isp::conv_quant_kernel<true, false><<<grid, 256, 0, stream>>>(p);
+  } else {
+    if (bf16) isp::conv_quant_kernel<false, true><<<grid, 256, 0, stream>>>(p);
+    else isp::conv_quant_kernel<false, false><<<grid, 256, 0, stream>>>(p);
+  }
+  return isp::launch_status();
+}
+
+int isp_conv1d(const void* xq, int ab_dtype, int64_t B, int C_pad, int64_t T_in, const void* w_packed, int CO,
+               int KW, int stride, int dilation, int padding, int output_padding, int transposed, int64_t T_out,
+               float in_scale, const float* amax, const float* w_scale, const float* bias, void* y, int out_dtype,
+               isp_stream_t stream) {
+  using namespace isp::gemm;
+  if (xq == nullptr || w_packed == nullptr || y == nullptr || w_scale == nullptr) return ISP_ERR_ARG;
+  if (ab_dtype != ISP_E4M3 && ab_dtype != ISP_I8) return ISP_ERR_DTYPE;
+  if (out_dtype != ISP_F32 && out_dtype != ISP_BF16 && out_dtype != ISP_F16) return ISP_ERR_DTYPE;
+  if (amax != nullptr ? (ab_dtype != ISP_E4M3 || in_scale != 0.f) : !(in_scale > 0.f)) return ISP_ERR_ARG;
+  ConvGeom g;
+  if (int st = conv_geometry(KW, stride, dilation, padding, transposed, &g)) return st;
+  if (B < 0 || B > 0xFFFF || C_pad <= 0 || C_pad % 128 != 0 || T_in <= 0 || CO <= 0 || output_padding < 0 ||
+      T_in > 0x3FFFFFFFll || T_out > 0x3FFFFFFFll)
+    return ISP_ERR_SHAPE;
+  const int64_t expect = transposed ? (T_in - 1) * stride - 2 * static_cast<int64_t>(padding) +
+                                          static_cast<int64_t>(dilation) * (KW - 1) + output_padding + 1
+                                    : (T_in + 2 * static_cast<int64_t>(padding) -
+                                       static_cast<int64_t>(dilation) * (KW - 1) - 1) / stride + 1;
+  if (T_out != expect || T_out <= 0 || (!transposed && output_padding != 0)) return ISP_ERR_SHAPE;
+  const int cblocks = C_pad / kBK;
+  if (g.a_stride * cblocks > 1023) return ISP_ERR_SHAPE;
+  if (!isp::aligned16(xq) || !isp::aligned16(w_packed) || !isp::aligned16(w_scale) ||
+      (bias && !isp::aligned16(bias)))
+    return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  if (B == 0) return ISP_OK;
+  const int64_t k_bytes = static_cast<int64_t>(g.taps) * C_pad;
+  const int64_t t_rows = (T_in + g.a_stride - 1) / g.a_stride;   // rows of the A view per utterance
+  const int64_t q_rows = (T_out + g.phases - 1) / g.phases;      // output rows of phase 0
+  const int tpb = static_cast<int>((q_rows + kBM - 1) / kBM);
+  const int ntco = (CO + kBN - 1) / kBN;
+  if (k_bytes > 0x7FFFFFFFll || static_cast<int64_t>(B) * tpb * kBM > 0x7FFFFFFFll ||
+      static_cast<int64_t>(B) * tpb * g.phases * ntco > 0x7FFFFFFFll)
+    return ISP_ERR_SHAPE;
+  CUtensorMap ta, tb;
+  if (!make_map3d_u8(&ta, xq, static_cast<uint64_t>(g.a_stride) * C_pad, static_cast<uint64_t>(t_rows),
+                     static_cast<uint64_t>(B), kBK, kBM) ||
+      !make_map3d_u8(&tb, w_packed, static_cast<uint64_t>(k_bytes), static_cast<uint64_t>(CO),
+                     static_cast<uint64_t>(g.phases), kBK, kBN))
+    return ISP_ERR_ALIGN;
+  Params p{};
+  p.conv_tpb = tpb;
+  p.conv_ntco = ntco;
+  p.conv_phases = g.phases;
+  p.conv_taps = g.taps;
+  p.conv_cblocks = cblocks;
+  p.conv_tout = T_out;
+  p.conv_amax = amax;
+  for (int i = 0; i < g.phases * g.taps; ++i) p.conv_tab[i] = g.row[i] * 1024 + g.colstep[i] * cblocks;
+  p.M = static_cast<int>(B * tpb * kBM);
+  p.N = CO;
+  p.K = static_cast<int>(k_bytes);
+  p.m_tiles = static_cast<int>(B * tpb);
+  p.n_tiles = g.phases * ntco;
+  p.k_blocks = g.taps * cblocks;
+  p.a_scale = amax != nullptr ? 1.f : in_scale;   // dynamic: the epilogue applies the utterance's scale
+  p.w_scale = w_scale;
+  p.bias = bias;
+  p.out = y;
+  const bool stat = k_bytes <= kStatK && !streaming_forced();
+  if (ab_dtype == ISP_I8) {
+    switch (out_dtype) {
+      case ISP_F32: return launch_conv<AB_I8, OUT_F32>(stat, ta, tb, p, stream);
+      case ISP_F16: return launch_conv<AB_I8, OUT_F16>(stat, ta, tb, p, stream);
+      default: return launch_conv<AB_I8, OUT_BF16>(stat, ta, tb, p, stream);
+    }
+  }
+  switch (out_dtype) {
+    case ISP_F32: return launch_conv<AB_E4M3, OUT_F32>(stat, ta, tb, p, stream);
+    case ISP_F16: return launch_conv<AB_E4M3, OUT_F16>(stat, ta, tb, p, stream);
+    default: return launch_conv<AB_E4M3, OUT_BF16>(stat, ta, tb, p, stream);
+  }
 }
 
 int isp_fir_snake(const float* x, int64_t rows, int C, int64_t T, const float* up,

@@ -105,6 +105,32 @@ def main(reference_root: str):
                          eps=np.float32(1e-6), ada_w=w.reshape(4, 512).numpy(), ada_b=b.reshape(4, 512).numpy(),
                          rows_per_group=np.int64(64), scale=np.float32(scale), y=y.numpy(), codes=_fp8_codes(codes)))
 
+    # --- learned Conv1d / ConvTranspose1d through ExportWeightOp (FP8 Q/DQ, FP32 conv) --
+    gc = torch.Generator().manual_seed(11)
+    conv = torch.nn.Conv1d(64, 48, 7, padding=9, dilation=3)
+    deconv = torch.nn.ConvTranspose1d(32, 24, 8, stride=4, padding=2)
+    with torch.no_grad():
+        for mod in (conv, deconv):
+            mod.weight.copy_(torch.randn(mod.weight.shape, generator=gc) * 0.05)
+            mod.bias.copy_(torch.randn(mod.bias.shape, generator=gc) * 0.1)
+        xc = torch.randn(2, 64, 40, generator=gc)
+        xd = torch.randn(2, 32, 20, generator=gc)
+        sc = conv.weight.abs().amax(dim=(1, 2)) / 448
+        sd = deconv.weight.abs().amax(dim=(0, 2)) / 448
+        op_c = ExportWeightOp(conv, {"precision": "fp8", "input_scale": float(xc.abs().max()) / 448,
+                                     "weight_scale": sc.tolist(), "weight_axis": 0})
+        op_d = ExportWeightOp(deconv, {"precision": "fp8", "input_scale": float(xd.abs().max()) / 448,
+                                       "weight_scale": sd.tolist(), "weight_axis": 1,
+                                       "conv_transpose_rewrite": "zero_insert_conv"})
+        yc, yd = op_c(xc), op_d(xd)
+    written.append(_save("conv_fp8_export", x=xc.numpy(), w=conv.weight.detach().numpy(),
+                         bias=conv.bias.detach().numpy(),
+                         in_scale=np.float32(op_c.input_scale), w_scale=op_c.weight_scale.numpy(),
+                         dilation=np.int64(3), padding=np.int64(9), y=yc.numpy(),
+                         xd=xd.numpy(), wd=deconv.weight.detach().numpy(), biasd=deconv.bias.detach().numpy(),
+                         in_scale_d=np.float32(op_d.input_scale), w_scale_d=op_d.weight_scale.numpy(),
+                         stride_d=np.int64(4), padding_d=np.int64(2), yd=yd.numpy()))
+
     # --- Zipformer BiasNorm (FP32) + ZipVoice export_qdq ------------------------------
     xf = activations(192, 512, 5, 10.0, 2)
     bn = BiasNorm(512)
@@ -221,6 +247,15 @@ def main(reference_root: str):
                          alpha=snake_act.act.alpha.detach().numpy(),
                          log_alpha=beta_act.act.alpha.detach().numpy(), log_beta=beta_act.act.beta.detach().numpy(),
                          **cases))
+
+    # the reference's FP8 Triton kernels, through Triton's CPU interpreter (own process:
+    # the interpreter is switched on by an environment variable read at import)
+    import os
+    import subprocess
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join(sys.path[:2] + [os.environ.get("PYTHONPATH", "")]))
+    out = subprocess.run([sys.executable, str(HERE / "make_golden_triton.py"), reference_root], env=env, check=True,
+                         capture_output=True, text=True).stdout
+    written += [HERE / name for name in out.split()]
 
     lines = [f"{hashlib.sha256(p.read_bytes()).hexdigest()}  {p.name}" for p in sorted(written)]
     (HERE / "MANIFEST.sha256").write_text("\n".join(lines) + "\n")

@@ -151,3 +151,63 @@ def test_fir_static_alias_free_and_snakebeta():
     inv_beta = (np.float32(1) / (np.exp(d["log_beta"]).astype(np.float32) + np.float32(1e-9))).astype(np.float32)
     y = fir.alias_free_snake(d["x_301"], d["up"], d["down"], alpha, inv_beta)
     assert rel_l2(y, d["y_beta_301"]) < 1e-6
+
+
+def test_conv_oracle_matches_export_weight_op():
+    """Quantized learned Conv1d and ConvTranspose1d (zero-insertion rewrite) of the
+    reference's export graph, against the oracle's exact-sum restatement."""
+    from oracle import conv as oconv
+    d = load("conv_fp8_export")
+    y = oconv.fp8_conv1d(d["x"], d["w"], d["bias"], d["in_scale"], d["w_scale"], dilation=int(d["dilation"]),
+                         padding=int(d["padding"]))
+    assert y.shape == d["y"].shape
+    assert np.linalg.norm(y - d["y"]) / np.linalg.norm(d["y"]) < 1e-6      # torch's FP32 conv sum order
+    yd = oconv.fp8_conv_transpose1d(d["xd"], d["wd"], d["biasd"], d["in_scale_d"], d["w_scale_d"],
+                                    stride=int(d["stride_d"]), padding=int(d["padding_d"]))
+    assert yd.shape == d["yd"].shape
+    assert np.linalg.norm(yd - d["yd"]) / np.linalg.norm(d["yd"]) < 1e-6
+
+
+CONV_MATRIX_CASES = ("dilated", "strided", "deconv", "deconv_ragged", "bf16")
+
+
+@pytest.mark.parametrize("name", CONV_MATRIX_CASES)
+def test_matrix_conv_oracle_matches_triton_reference(name):
+    """``ops/triton/fp8_conv.conv1d`` (run by Triton's CPU interpreter on exact
+    E4M3 inputs) against the oracle's gather-form restatement: every geometry,
+    dynamic per-utterance scales, the packed [K, N] weight."""
+    from oracle import conv as oconv
+    d = load("conv_matrix_fp8")
+    tr, ci, co, kw, s, pad, dil, op, bf = (int(v) for v in d[f"{name}_geom"])
+    bias = d[f"{name}_bias"] if f"{name}_bias" in d.files else None
+    y = oconv.matrix_conv1d(d[f"{name}_x"], d[f"{name}_packed"], d[f"{name}_scales"], bias, ci, co, kw, s, pad, dil,
+                            bool(tr), op)
+    ref = d[f"{name}_y"]
+    assert y.shape == ref.shape
+    if bf:
+        # the interpreter's BF16 store truncates; the FP32 value before it must agree
+        assert np.array_equal((y.view(np.uint32) & 0xFFFF0000).view(np.float32), ref)
+    else:
+        assert rel_l2(y, ref) < 1e-6                                      # FP32 dot order of the interpreter
+
+
+def test_matrix_conv_weight_packing_is_pack_weight():
+    """The packed conv weight is ``pack_weight`` of the [CO, CI * KW] matrix
+    (ConvTranspose1d: of weight.permute(1, 0, 2))."""
+    d = load("conv_matrix_fp8")
+    for name in CONV_MATRIX_CASES:
+        tr, ci, co, kw = (int(v) for v in d[f"{name}_geom"][:4])
+        w = d[f"{name}_w"]
+        dense = np.transpose(w, (1, 0, 2)) if tr else w
+        packed, scales = gemm.pack_weight(dense.reshape(co, ci * kw))
+        assert np.array_equal(packed, d[f"{name}_packed"]), name
+        assert np.array_equal(scales, d[f"{name}_scales"]), name
+
+
+def test_fp8_linear_oracle_matches_triton_reference():
+    """``ops/triton/fp8.linear`` (dynamic per-row scale; single and split-K
+    tiles) on exact E4M3 inputs against ``oracle.gemm.fp8_linear``."""
+    d = load("fp8_linear_triton")
+    y = gemm.fp8_linear(d["x"], d["packed"], d["scales"], d["bias"], out_bf16=False)
+    for split in (1, 3):
+        assert rel_l2(y, d[f"y_split{split}"]) < 1e-6
