@@ -377,6 +377,45 @@ def run_case(args, torch, device, hbm_peak, bf16_peak):
             nbytes = m * k // 2 + sf_bytes(m, k) + rows_w * k // 2 + m * n * 2
             flops = 2 * m * n * k
             name = f"nvfp4 gemm M={m} N={n} K={k} -> BF16"
+    elif args.case in ("conv", "deconv", "conv_quant"):
+        # BigVGAN learned convolutions next to the cfg-5 FIR: a resblock Conv1d(512, 512, 3,
+        # dilation 3) at T=16384 and an upsampling ConvTranspose1d(512, 256, 8, stride 4) to
+        # T=16384, B=16, FP32 in/out, dynamic per-utterance E4M3 scale (ops/triton/fp8_conv.py)
+        from inspark_proper_format_b200 import conv as iconv
+        b = 16
+        if args.case == "deconv":
+            tr, ci, co, kw, st, pad, dil, t = True, 512, 256, 8, 4, 2, 1, 4096
+        else:
+            tr, ci, co, kw, st, pad, dil, t = False, 512, 512, 3, 1, 3, 3, 16384
+        x = torch.randn(b, ci, t, device=device, generator=g)
+        w = torch.randn(ci, co, kw, device=device, generator=g) * 0.05 if tr else \
+            torch.randn(co, ci, kw, device=device, generator=g) * 0.05
+        dense = w.permute(1, 0, 2) if tr else w
+        from inspark_proper_format_b200.gemm import pack_weight
+        packed, scales = pack_weight(dense.reshape(co, ci * kw))
+        folded = iconv.pack_folded(packed.view(torch.uint8), co, ci, kw, st, dil, pad, tr)
+        phases, taps = iconv.geometry(kw, st, dil, pad, tr)
+        t_out = iconv.out_length(t, kw, st, pad, dil, tr)
+        c_pad = folded.shape[-1]
+        xq = torch.empty(b, t, c_pad, device=device, dtype=torch.uint8)
+        amax = torch.empty(b, device=device)
+        y = torch.empty(b, co, t_out, device=device)
+        bias = torch.rand(co, device=device, generator=g)
+        qargs = (x.data_ptr(), _lib.F32, b, ci, t, 1, None, 0.0, amax.data_ptr(), _lib.E4M3, xq.data_ptr(), c_pad,
+                 stream)
+        _lib.check(lib.isp_conv1d_quant(*qargs), "isp_conv1d_quant")
+        if args.case == "conv_quant":
+            fn, fargs = lib.isp_conv1d_quant, qargs
+            nbytes, flops = b * ci * t * 8 + b * t * c_pad, 0     # x read by the amax and the quant pass
+            name = f"conv input amax + quant [{b},{ci},{t}] FP32 -> E4M3 channels-last (3 launches)"
+        else:
+            fn = lib.isp_conv1d
+            fargs = (xq.data_ptr(), _lib.E4M3, b, c_pad, t, folded.data_ptr(), co, kw, st, dil, pad, 0, int(tr), t_out,
+                     0.0, amax.data_ptr(), scales.data_ptr(), bias.data_ptr(), y.data_ptr(), _lib.F32, stream)
+            nbytes = b * t * c_pad + folded.numel() + b * co * t_out * 4
+            flops = 2 * b * t_out * co * ci * (kw // st if tr else kw)     # useful products (no zero taps)
+            kind = f"ConvTranspose1d({ci},{co},{kw},s={st})" if tr else f"Conv1d({ci},{co},{kw},d={dil})"
+            name = f"{kind} B{b} T_in={t} T_out={t_out} E4M3 -> FP32, {phases} folded phase(s) x {taps} window slots"
     else:
         import ctypes
 
@@ -496,6 +535,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-components", action="store_true")
     ap.add_argument("--case", choices=("stack", "gemm", "norm_quant", "fir", "nvfp4_gated_up", "nvfp4_down",
+                                       "conv", "deconv", "conv_quant",
                                        "int8_decode"),
                     default="stack",
                     help="stack = the headline step; the others time one kernel (profiling targets)")

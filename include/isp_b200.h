@@ -138,13 +138,14 @@ int isp_adaln_quant(const void *x, int x_dtype, int64_t M, int K, const float *g
 int isp_nvfp4_scales_to_mma(const void *src, int64_t R, int K, void *dst, isp_stream_t stream);
 
 /*
- * Quantized learned convolutions (groups 1, zero padding) as a polyphase
- * implicit GEMM on tcgen05.  A Conv1d (stride S) is one phase whose K blocks
- * are (tap, 128 channels) boxes of channels-last codes; a ConvTranspose1d
- * (stride S) is S phases, phase r producing output times q * S + r from the
- * taps with tap * dilation = r + padding (mod S) -- the same products as the
- * reference's zero-insertion rewrite and its gather kernel, without the
- * (S - 1) / S zero rows.  Three calls: pack the weight once, quantize the
+ * Quantized learned convolutions (groups 1, zero padding) as one phase-folded
+ * implicit GEMM on tcgen05.  Conv1d (stride S): rows are output times, K runs
+ * over (tap, 128 channels) boxes of channels-last codes.  ConvTranspose1d
+ * (stride S): output time q * S + r is row q and column co * S + r, and K runs
+ * over the window of input rows q + R that any phase reads, so every product of
+ * the reference's zero-insertion rewrite and gather kernel is formed once,
+ * without the (S - 1) / S zero rows (taps that do not reach a (phase, row)
+ * pair are zero weights).  Three calls: pack the weight once, quantize the
  * input, run the convolution.
  *
  * Replaces: ops/triton/fp8_conv.py:24-62 (conv1d, the FP8 MatrixConv path of
@@ -153,8 +154,8 @@ int isp_nvfp4_scales_to_mma(const void *src, int64_t R, int K, void *dst, isp_st
  *   156-216, static FP8 / INT8 SmoothQuant Q/DQ, zero-insertion rewrite).
  */
 
-/* Phase count and taps per phase of a convolution geometry (for sizing the
- * packed weight [phases, CO, taps, C_pad]).  phases * taps <= 128. */
+/* Phases P (1, or the ConvTranspose1d stride) and window slots W of a geometry,
+ * for sizing the packed weight [CO * P, W, C_pad].  W <= 128. */
 int isp_conv1d_geometry(int KW, int stride, int dilation, int padding, int transposed,
                         int *phases, int *taps);
 
@@ -163,7 +164,7 @@ int isp_conv1d_geometry(int KW, int stride, int dilation, int padding, int trans
  * co: the packed [K, N] layout of quantization/weights.py:5-17, whose per-
  * output-channel scales are used unchanged; for ConvTranspose1d the rows come
  * from weight.permute(1, 0, 2) as in quantization/precision.py:34-36) ->
- * w_packed [phases, CO, taps, C_pad], zero past CI and in empty tap slots.
+ * w_packed [CO * P, W, C_pad], zero past CI and where no tap reaches.
  * ldw >= CO; C_pad % 128 == 0, C_pad >= CI; w_packed 16-byte aligned.
  */
 int isp_conv1d_pack_weight(const void *codes, int64_t ldw, int CO, int CI, int KW, int stride,

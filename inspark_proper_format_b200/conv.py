@@ -1,4 +1,4 @@
-"""Quantized learned convolutions on tcgen05: a polyphase implicit GEMM over
+"""Quantized learned convolutions on tcgen05: a phase-folded implicit GEMM over
 channels-last codes (``isp_conv1d_pack_weight`` / ``isp_conv1d_quant`` /
 ``isp_conv1d``).
 
@@ -13,7 +13,7 @@ Reference surfaces mirrored here:
   * ``ExportWeightOp`` for ``nn.Conv1d`` / ``nn.ConvTranspose1d`` roles with an
     FP8 or INT8 spec (``build/unified_acoustic_export.py:75-216``): static input
     scale, INT8 SmoothQuant folded into the weight, ConvTranspose1d through the
-    zero-insertion rewrite -> ``QuantConv1d``.  The polyphase form multiplies
+    zero-insertion rewrite -> ``QuantConv1d``.  The phase-folded form multiplies
     the same code pairs as that rewrite and skips its zero rows.
 Groups = 1 and zero padding, as the reference requires.
 """
@@ -45,34 +45,34 @@ def out_length(t: int, kw: int, stride: int, padding: int, dilation: int, transp
 
 
 def geometry(kw: int, stride: int, dilation: int, padding: int, transpose: bool) -> tuple[int, int]:
-    """(phases, taps per phase) of the polyphase form."""
+    """(phases P, window slots W) of the phase-folded form."""
     phases, taps = ctypes.c_int(), ctypes.c_int()
     _lib.check(_lib.load().isp_conv1d_geometry(kw, stride, dilation, padding, int(transpose), ctypes.byref(phases),
                                                ctypes.byref(taps)), "isp_conv1d_geometry")
     return phases.value, taps.value
 
 
-def pack_polyphase(codes_kn: torch.Tensor, co: int, ci: int, kw: int, stride: int, dilation: int, padding: int,
-                   transpose: bool) -> torch.Tensor:
+def pack_folded(codes_kn: torch.Tensor, co: int, ci: int, kw: int, stride: int, dilation: int, padding: int,
+                transpose: bool) -> torch.Tensor:
     """Weight codes [CI * KW, ldw] (row ci * KW + tap; E4M3 or INT8) -> the
-    polyphase B operand [phases, CO, taps, C_pad] on the codes' device."""
+    phase-folded B operand [CO * P, W, C_pad] on the codes' device."""
     codes = codes_kn.contiguous()
     if codes.dim() != 2 or codes.shape[0] != ci * kw or codes.shape[1] < co:
         raise ValueError("weight codes must be [CI * KW, >= CO]")
     phases, taps = geometry(kw, stride, dilation, padding, transpose)
     c_pad = _pad128(ci)
-    out = torch.empty(phases, co, taps, c_pad, device=codes.device, dtype=codes.dtype)
+    out = torch.empty(co * phases, taps, c_pad, device=codes.device, dtype=codes.dtype)
     _lib.check(_lib.load().isp_conv1d_pack_weight(codes.data_ptr(), codes.shape[1], co, ci, kw, stride, dilation,
                                                   padding, int(transpose), out.data_ptr(), c_pad,
                                                   _lib.stream_handle(codes.device)), "isp_conv1d_pack_weight")
     return out
 
 
-def run(x: torch.Tensor, w_poly: torch.Tensor, w_scale: torch.Tensor, bias: torch.Tensor | None, *, ci: int, co: int,
+def run(x: torch.Tensor, w_folded: torch.Tensor, w_scale: torch.Tensor, bias: torch.Tensor | None, *, ci: int, co: int,
         kw: int, stride: int, padding: int, dilation: int, transpose: bool, output_padding: int = 0,
         code: str = "fp8", in_scale: float | None = None, smooth: torch.Tensor | None = None,
         out_dtype: torch.dtype | None = None) -> torch.Tensor:
-    """Quantize x [B, CI, T] and run the polyphase conv.  in_scale None: the
+    """Quantize x [B, CI, T] and run the phase-folded conv.  in_scale None: the
     dynamic per-utterance E4M3 scale; else the static scale (INT8: x / smooth
     first)."""
     if x.dim() != 3 or x.shape[1] != ci:
@@ -87,7 +87,7 @@ def run(x: torch.Tensor, w_poly: torch.Tensor, w_scale: torch.Tensor, bias: torc
     if t_out <= 0:
         raise ValueError("Non-positive output extent")
     code_dtype = _CODES[code][0]
-    c_pad = w_poly.shape[-1]
+    c_pad = w_folded.shape[-1]
     row_multiple = 1 if transpose else stride
     t_rows = (t + row_multiple - 1) // row_multiple * row_multiple
     lib = _lib.load()
@@ -99,28 +99,28 @@ def run(x: torch.Tensor, w_poly: torch.Tensor, w_scale: torch.Tensor, bias: torc
                                     0.0 if in_scale is None else float(in_scale), _lib.ptr(amax), code_dtype,
                                     xq.data_ptr(), c_pad, stream), "isp_conv1d_quant")
     y = torch.empty(b, co, t_out, device=x.device, dtype=out_dtype)
-    _lib.check(lib.isp_conv1d(xq.data_ptr(), code_dtype, b, c_pad, t, w_poly.data_ptr(), co, kw, stride, dilation,
+    _lib.check(lib.isp_conv1d(xq.data_ptr(), code_dtype, b, c_pad, t, w_folded.data_ptr(), co, kw, stride, dilation,
                               padding, output_padding, int(transpose), t_out,
                               0.0 if in_scale is None else float(in_scale), _lib.ptr(amax), w_scale.data_ptr(),
                               _lib.ptr(bias), y.data_ptr(), _OUT[out_dtype], stream), "isp_conv1d")
     return y
 
 
-_POLY: dict = {}
+_FOLDED: dict = {}
 
 
-def _polyphase_cached(packed: torch.Tensor, co, ci, kw, stride, dilation, padding, transpose) -> torch.Tensor:
-    """pack_polyphase of a reference-packed weight, done once per tensor object
+def _folded_cached(packed: torch.Tensor, co, ci, kw, stride, dilation, padding, transpose) -> torch.Tensor:
+    """pack_folded of a reference-packed weight, done once per tensor object
     and geometry (invalidated when the tensor is freed or modified in place)."""
     key = (id(packed), co, ci, kw, stride, dilation, padding, bool(transpose))
-    hit = _POLY.get(key)
+    hit = _FOLDED.get(key)
     if hit is not None:
-        ref, version, poly = hit
+        ref, version, folded = hit
         if ref() is packed and version == packed._version:
-            return poly
-    poly = pack_polyphase(packed.view(torch.uint8), co, ci, kw, stride, dilation, padding, transpose)
-    _POLY[key] = (weakref.ref(packed, lambda _r, k=key: _POLY.pop(k, None)), packed._version, poly)
-    return poly
+            return folded
+    folded = pack_folded(packed.view(torch.uint8), co, ci, kw, stride, dilation, padding, transpose)
+    _FOLDED[key] = (weakref.ref(packed, lambda _r, k=key: _FOLDED.pop(k, None)), packed._version, folded)
+    return folded
 
 
 def conv1d(x, weight, scales, bias, ci, co, kw, stride, padding, dilation, transpose, output_padding, tile=None):
@@ -130,8 +130,8 @@ def conv1d(x, weight, scales, bias, ci, co, kw, stride, padding, dilation, trans
     accepted for signature compatibility (one sm_100a schedule)."""
     if x.shape[1] != ci:
         raise ValueError("Input channels changed")
-    poly = _polyphase_cached(weight, co, ci, kw, stride, dilation, padding, transpose)
-    return run(x, poly, scales.float().contiguous(), None if bias is None else bias.float().contiguous(), ci=ci,
+    folded = _folded_cached(weight, co, ci, kw, stride, dilation, padding, transpose)
+    return run(x, folded, scales.float().contiguous(), None if bias is None else bias.float().contiguous(), ci=ci,
                co=co, kw=kw, stride=stride, padding=padding, dilation=dilation, transpose=transpose,
                output_padding=output_padding)
 
@@ -230,20 +230,20 @@ class QuantConv1d(nn.Module):
         self.input_scale = float(spec["input_scale"])
         if not self.input_scale > 0:
             raise ValueError("input_scale must be positive")
-        self._poly = None
+        self._folded = None
 
-    def polyphase_weight(self) -> torch.Tensor:
-        if self._poly is None or self._poly.device != self.weight_codes.device:
-            self._poly = pack_polyphase(self.weight_codes.view(torch.uint8), self.out_channels, self.in_channels,
+    def folded_weight(self) -> torch.Tensor:
+        if self._folded is None or self._folded.device != self.weight_codes.device:
+            self._folded = pack_folded(self.weight_codes.view(torch.uint8), self.out_channels, self.in_channels,
                                         self.kernel_size, self.stride, self.dilation, self.padding, self.transpose)
-        return self._poly
+        return self._folded
 
     def out_length(self, t: int) -> int:
         return out_length(t, self.kernel_size, self.stride, self.padding, self.dilation, self.transpose,
                           self.output_padding)
 
     def forward(self, x: torch.Tensor, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
-        return run(x, self.polyphase_weight(), self.weight_scale, self.bias, ci=self.in_channels,
+        return run(x, self.folded_weight(), self.weight_scale, self.bias, ci=self.in_channels,
                    co=self.out_channels, kw=self.kernel_size, stride=self.stride, padding=self.padding,
                    dilation=self.dilation, transpose=self.transpose, output_padding=self.output_padding,
                    code=self.precision, in_scale=self.input_scale, smooth=self.smooth_scale, out_dtype=out_dtype)

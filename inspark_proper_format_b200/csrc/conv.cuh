@@ -11,7 +11,7 @@
 //                      outside the utterance read as zero (the zero padding).
 //   conv_pack_kernel   per-output-channel weight codes [CI * KW, ldw] (the packed
 //                      [K, N] layout of quantization/weights.py:5-17) -> the
-//                      polyphase B operand [phases, CO, taps, C_pad].
+//                      phase-folded B operand [CO * phases, taps, C_pad].
 #pragma once
 
 #include "common.cuh"
@@ -101,28 +101,36 @@ __global__ void __launch_bounds__(256) conv_quant_kernel(ConvQuantParams p) {
 }
 
 // ---- weight packing ----------------------------------------------------------
+// B operand of the phase-folded GEMM: row co * P + r, K = (window slot j, channel c).
+// Conv1d (P = 1): slot j is tap j.  ConvTranspose1d (stride S = P): slot j reads input
+// row q + (r_min + j) for output time q * S + r, which tap k = (r + padding - (r_min + j)
+// * S) / dilation supplies when that division is exact and 0 <= k < KW; otherwise 0.
 struct ConvPackParams {
   const uint8_t* src;      // [CI * KW, ldw] codes, row ci * KW + tap, column co
   int64_t ldw;
   int CO, CI, KW;
   int phases, taps, c_pad;
-  uint8_t* dst;            // [phases, CO, taps, c_pad]
-  int tap[gemm::kConvTab]; // (phase, slot) -> kernel tap, -1 = zero slot
+  int transposed, stride, dilation, padding, r_min;
+  uint8_t* dst;            // [CO * phases, taps, c_pad]
 };
 
-// One thread per 16 destination bytes (16 channels of one (phase, co, slot)).
-__global__ void __launch_bounds__(256) conv_pack_kernel(const __grid_constant__ ConvPackParams p) {
+// One thread per 16 destination bytes (16 channels of one (row, slot)).
+__global__ void __launch_bounds__(256) conv_pack_kernel(ConvPackParams p) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int chunks = p.c_pad / 16;
-  const int64_t total = static_cast<int64_t>(p.phases) * p.CO * p.taps * chunks;
+  const int64_t total = static_cast<int64_t>(p.CO) * p.phases * p.taps * chunks;
   if (i >= total) return;
   const int chunk = static_cast<int>(i % chunks);
   int64_t rest = i / chunks;
   const int slot = static_cast<int>(rest % p.taps);
-  rest /= p.taps;
-  const int co = static_cast<int>(rest % p.CO);
-  const int r = static_cast<int>(rest / p.CO);
-  const int tap = p.tap[r * p.taps + slot];
+  const int64_t row = rest / p.taps;
+  const int co = static_cast<int>(row / p.phases);
+  const int r = static_cast<int>(row % p.phases);
+  int tap = slot;
+  if (p.transposed) {
+    const int64_t num = static_cast<int64_t>(r) + p.padding - static_cast<int64_t>(p.r_min + slot) * p.stride;
+    tap = (num >= 0 && num % p.dilation == 0 && num / p.dilation < p.KW) ? static_cast<int>(num / p.dilation) : -1;
+  }
   uint32_t w[4] = {0u, 0u, 0u, 0u};
   if (tap >= 0) {
 #pragma unroll

@@ -50,9 +50,10 @@ struct Roles {
 };
 
 enum AbKind { AB_E4M3 = 0, AB_I8 = 1, AB_FP4 = 2 };
-// EPI_CONV: the scale epilogue of a polyphase implicit-GEMM convolution (A rows =
-// output times of one phase of one utterance, A gathered per (tap, 128-channel)
-// block from channels-last codes; output stored transposed to [B, CO, T_out]).
+// EPI_CONV: the scale epilogue of a phase-folded implicit-GEMM convolution (A rows =
+// phase rows of one utterance, A gathered per (window slot, 128-channel) block from
+// channels-last codes; column co * P + r is output channel co at phase r; output
+// stored transposed to [B, CO, T_out]).
 enum EpiKind { EPI_SCALE = 0, EPI_SWIGLU_PAIRED = 1, EPI_SWIGLU_INTERLEAVED = 2, EPI_CONV = 3 };
 // OUT_NVFP4: packed E2M1 codes + E4M3 block scales in the tensor-core layout.
 enum OutKind { OUT_BF16 = 0, OUT_F16 = 1, OUT_F32 = 2, OUT_E4M3 = 3, OUT_NVFP4 = 4 };
@@ -91,19 +92,21 @@ struct Params {
   float q_scale;          // NVFP4 output: global scale of h
   uint8_t* q_codes;       // NVFP4 output: packed E2M1 [M, N/2]
   uint8_t* q_sf;          // NVFP4 output: block scales, tensor-core layout
-  // EPI_CONV (polyphase implicit-GEMM Conv1d / ConvTranspose1d):
+  // EPI_CONV (phase-folded implicit-GEMM Conv1d / ConvTranspose1d, P = conv_phases):
   //   m tile mt -> utterance mt / conv_tpb, first phase row q0 = (mt % conv_tpb) * 128;
-  //   n tile nt -> phase r = nt / conv_ntco, output channels (nt % conv_ntco) * kBN;
-  //   K block kb -> table entry e = conv_tab[r * conv_taps + kb / conv_cblocks]: the A box
-  //   starts at row q0 + (e >> 10) and 128-byte column ((e & 1023) + kb % conv_cblocks);
-  //   phase row q of phase r is output time q * conv_phases + r.
+  //   column n (N = CO * P) -> output channel n / P, phase r = n % P; phase row q of
+  //   phase r is output time q * P + r;
+  //   K block kb -> window slot j = kb / conv_cblocks, e = conv_tab[j]: the A box starts
+  //   at row q0 + (e >> 10) and 128-byte column ((e & 1023) + kb % conv_cblocks).
   int conv_tpb;
-  int conv_ntco;
   int conv_phases;
   int conv_taps;
   int conv_cblocks;
+  int conv_co;
   int64_t conv_tout;
   const float* conv_amax; // per-utterance |x| max (dynamic input scale) or nullptr
+  int conv_tma_store;     // 1: output blocks of 32 rows x 32 columns leave through the
+                          // [B, CO, T_out] tensor map (boxes of 32/P channels x 32P times)
   int conv_tab[kConvTab];
 };
 
@@ -229,6 +232,12 @@ ISP_D void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* 
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_u32(smem_dst)),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+ISP_D void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
                : "memory");
 }
 ISP_D void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -385,6 +394,59 @@ ISP_D uint32_t pack_f16(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+// ---- EPI_CONV output staging ----
+template <int kN>
+ISP_D void st_shared_words(uint8_t* dst, const uint32_t (&w)[kN]) {
+  if constexpr (kN == 1) {
+    *reinterpret_cast<uint32_t*>(dst) = w[0];
+  } else if constexpr (kN == 2) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < kN; i += 4)
+      *reinterpret_cast<uint4*>(dst + 4 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+  }
+}
+
+// One lane's 32 values (columns c * P + r of its phase row q) -> the output box
+// [32/P channels][32 rows x P times] (times contiguous): the lane's P values of
+// channel c are consecutive times q * P .. q * P + P - 1, written as one vector at
+// c * 32P + q * P, so a warp's store covers a contiguous run (no bank conflicts).
+template <int kOut, int kP>
+ISP_D void stage_conv_box_p(uint8_t* sb, int lane, const float (&v)[32]) {
+  constexpr int kEb = kOut == OUT_F32 ? 4 : 2;
+#pragma unroll
+  for (int c = 0; c < 32 / kP; ++c) {
+    uint8_t* dst = sb + (c * 32 * kP + lane * kP) * kEb;
+    if constexpr (kEb == 4) {
+      uint32_t w[kP];
+#pragma unroll
+      for (int r = 0; r < kP; ++r) w[r] = __float_as_uint(v[c * kP + r]);
+      st_shared_words<kP>(dst, w);
+    } else if constexpr (kP == 1) {
+      *reinterpret_cast<uint16_t*>(dst) = kOut == OUT_F16 ? __half_as_ushort(__float2half_rn(v[c]))
+                                                          : __bfloat16_as_ushort(__float2bfloat16_rn(v[c]));
+    } else {
+      uint32_t w[kP / 2];
+#pragma unroll
+      for (int i = 0; i < kP / 2; ++i)
+        w[i] = kOut == OUT_F16 ? pack_f16(v[c * kP + 2 * i], v[c * kP + 2 * i + 1])
+                               : pack_bf16(v[c * kP + 2 * i], v[c * kP + 2 * i + 1]);
+      st_shared_words<kP / 2>(dst, w);
+    }
+  }
+}
+
+template <int kOut>
+ISP_D void stage_conv_box(uint8_t* sb, int lane, int phases, const float (&v)[32]) {
+  switch (phases) {
+    case 1: stage_conv_box_p<kOut, 1>(sb, lane, v); break;
+    case 2: stage_conv_box_p<kOut, 2>(sb, lane, v); break;
+    case 4: stage_conv_box_p<kOut, 4>(sb, lane, v); break;
+    default: stage_conv_box_p<kOut, 8>(sb, lane, v); break;
+  }
+}
+
 // satfinite saturates +-inf and out-of-range values to +-448 and keeps NaN,
 // the same result as the reference's clamp(-448, 448) followed by the cast.
 ISP_D uint32_t pack_e4m3x4(float a, float b, float c, float d) {
@@ -433,13 +495,6 @@ ISP_D void lds32(const float* p, float (&v)[32]) {   // uniform address: a broad
 // Columns at or past N read as 0, so the math needs no column guards.
 // For EPI_SCALE with a per-tensor activation scale the staged column scale is
 // already sa * w_scale[n] (the product the INT8 reference forms as AS * WS[n]).
-// First output column of n tile nt (EPI_CONV: tiles of every phase cover the same channels).
-template <int kEpi, int kOutCols>
-ISP_D int tile_col0(const Params& p, int nt) {
-  if constexpr (kEpi == EPI_CONV) return (nt % p.conv_ntco) * kOutCols;
-  return nt * kOutCols;
-}
-
 template <int kEpi, int kBN, int kEpiThreads>
 struct TileParams {
   static constexpr int kPer = 256 / kEpiThreads;
@@ -453,9 +508,10 @@ struct TileParams {
       if constexpr (kEpi == EPI_SCALE || kEpi == EPI_CONV) {
         const int n = n0 + i;
         if (i < kBN && n < p.N) {
-          x = p.w_scale != nullptr ? __ldg(p.w_scale + n) : 1.f;
+          const int c = kEpi == EPI_CONV ? n / p.conv_phases : n;   // EPI_CONV: column -> channel
+          x = p.w_scale != nullptr ? __ldg(p.w_scale + c) : 1.f;
           if (p.a_scale_rows == nullptr) x = __fmul_rn(p.a_scale, x);
-          y = p.bias != nullptr ? __ldg(p.bias + n) : 0.f;
+          y = p.bias != nullptr ? __ldg(p.bias + c) : 0.f;
         }
       } else if constexpr (kEpi == EPI_SWIGLU_PAIRED) {
         const int n = n0 + (i & 127);
@@ -782,11 +838,6 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         int mt, nt;
         S::coords(p, t, mt, nt);
         const int m0 = mt * kBM;
-        int cr = 0, cnt = nt;                    // EPI_CONV: phase and output-channel tile
-        if constexpr (kEpi == EPI_CONV) {
-          cr = nt / p.conv_ntco;
-          cnt = nt - cr * p.conv_ntco;
-        }
         if constexpr (kStat) {
           if (nt != cur_nt) {
             // reload the resident B tile once every MMA reading the previous one completed
@@ -799,8 +850,6 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
               if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
                 tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * (kBN / 2));
                 tma_load_2d(dst + (kBN / 2) * kBK, &tm_b2, bfull_bar, kb * kBK, nt * (kBN / 2));
-              } else if constexpr (kEpi == EPI_CONV) {
-                tma_load_3d(dst, &tm_b, bfull_bar, kb * kBK, cnt * kBN, cr);
               } else {
                 tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * kBN);
               }
@@ -827,7 +876,7 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
             if constexpr (kEpi == EPI_CONV) {
               const int b = mt / p.conv_tpb;
               const int j = kb / p.conv_cblocks;
-              const int e = p.conv_tab[cr * p.conv_taps + j];
+              const int e = p.conv_tab[j];
               const int q0 = (mt - b * p.conv_tpb) * kBM;
               tma_load_3d(sa, &tm_a, &full_bar[stage], ((e & 1023) + kb - j * p.conv_cblocks) * kBK, q0 + (e >> 10), b);
             } else {
@@ -842,8 +891,6 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
               if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
                 tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * (kBN / 2));
                 tma_load_2d(sb + (kBN / 2) * kBK, &tm_b2, &full_bar[stage], kb * kBK, nt * (kBN / 2));
-              } else if constexpr (kEpi == EPI_CONV) {
-                tma_load_3d(sb, &tm_b, &full_bar[stage], kb * kBK, cnt * kBN, cr);
               } else {
                 tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * kBN);
               }
@@ -1007,13 +1054,13 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
       if (sched.begin < sched.end) {
         int mt, nt;
         S::coords(p, sched.begin, mt, nt);
-        tp.fetch(p, tile_col0<kEpi, kOutCols>(p, nt), et);
+        tp.fetch(p, nt * kOutCols, et);
       }
       for (int t = sched.begin; t < sched.end; t += sched.step) {
         int mt, nt;
         S::coords(p, t, mt, nt);
         const int m0 = mt * kBM;
-        const int n0 = tile_col0<kEpi, kOutCols>(p, nt);
+        const int n0 = nt * kOutCols;
         // Per-column parameters of this tile -> shared memory (zero past column N),
         // then start fetching the next tile's.
         epilogue_sync<R::kEpiThreads>();
@@ -1022,17 +1069,15 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         if (t + sched.step < sched.end) {
           int mt2, nt2;
           S::coords(p, t + sched.step, mt2, nt2);
-          tp.fetch(p, tile_col0<kEpi, kOutCols>(p, nt2), et);
+          tp.fetch(p, nt2 * kOutCols, et);
         }
         if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
         tc_fence_after();
         const int m = m0 + row_in_tile;
-        // EPI_CONV: the row is phase row q of phase nt / conv_ntco, output time ct of utterance cu
+        // EPI_CONV: the row is phase row cq of utterance cu (output times cq * P + r)
         const int cu = kEpi == EPI_CONV ? mt / p.conv_tpb : 0;
-        const int64_t ct = kEpi == EPI_CONV ? (static_cast<int64_t>(mt - cu * p.conv_tpb) * kBM + row_in_tile) *
-                                                      p.conv_phases + nt / p.conv_ntco
-                                            : 0;
-        const bool row_ok = kEpi == EPI_CONV ? ct < p.conv_tout : m < p.M;
+        const int64_t cq = kEpi == EPI_CONV ? static_cast<int64_t>(mt - cu * p.conv_tpb) * kBM + row_in_tile : 0;
+        const bool row_ok = kEpi == EPI_CONV ? cq * p.conv_phases < p.conv_tout : m < p.M;
         float sa = p.a_scale;
         if (p.a_scale_rows != nullptr && row_ok) sa = __ldg(p.a_scale_rows + m);
         if constexpr (kEpi == EPI_CONV)
@@ -1063,19 +1108,35 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
           if constexpr (kEpi == EPI_CONV) {
             if (p.conv_amax != nullptr) scale_group<kInt8, true>(ca, sa, params + col, params + 256 + col, v);
             else scale_group<kInt8, false>(ca, sa, params + col, params + 256 + col, v);
-            // transposed direct store to [B, CO, T_out]: for each channel the 32 lanes
-            // write 32 times conv_phases apart (one 128-byte row segment for FP32 and
-            // one phase; the other phases' tiles fill the gaps)
-            if (row_ok) {
-              const int64_t base = static_cast<int64_t>(cu) * p.N * p.conv_tout + ct;
+            if (p.conv_tma_store) {
+              // this warp's 32 rows x 32 columns = 32/P channels x 32P consecutive times,
+              // staged channel-major (times contiguous) and stored as one box
+              if (lane == 0) bulk_wait_read_all();      // the previous box has left the buffer
+              __syncwarp();
+              stage_conv_box<kOut>(stage_base, lane, p.conv_phases, v);
+              fence_proxy_async_smem();
+              __syncwarp();
+              const int64_t t_first = (cq - lane) * p.conv_phases;
+              if (lane == 0 && t_first < p.conv_tout && n < p.N) {
+                tma_store_3d(&tm_out, stage_base, static_cast<int>(t_first), n / p.conv_phases, cu);
+                bulk_commit();
+              }
+            } else if (row_ok) {
+              // per-element stores to [B, CO, T_out]: column n + j is channel (n + j) / P at
+              // time cq * P + (n + j) % P
+              int co = n / p.conv_phases;
+              int r = n - co * p.conv_phases;
+              const int64_t tq = cq * p.conv_phases;
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
-                if (n + j < p.N) {
-                  const int64_t off = base + static_cast<int64_t>(n + j) * p.conv_tout;
+                const int64_t t = tq + r;
+                if (co < p.conv_co && t < p.conv_tout) {
+                  const int64_t off = (static_cast<int64_t>(cu) * p.conv_co + co) * p.conv_tout + t;
                   if constexpr (kOut == OUT_F32) static_cast<float*>(p.out)[off] = v[j];
                   else if constexpr (kOut == OUT_F16) static_cast<__half*>(p.out)[off] = __float2half_rn(v[j]);
                   else static_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(v[j]);
                 }
+                if (++r == p.conv_phases) { r = 0; ++co; }
               }
             }
             if (g + 1 < kGroups) {

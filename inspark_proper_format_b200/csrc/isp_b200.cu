@@ -93,6 +93,24 @@ bool make_map3d_u8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [B, CO, T_out] convolution output: boxes of 32/P channels x 32P times (one epilogue
+// warp's 32 phase rows x 32 folded columns), no swizzle.
+bool make_conv_out_map(CUtensorMap* map, void* y, int out_kind, uint64_t t_out, uint64_t co, uint64_t b,
+                       uint32_t phases) {
+  EncodeFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const int eb = out_bytes(out_kind);
+  const CUtensorMapDataType dt = out_kind == OUT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : out_kind == OUT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {t_out, co, b};
+  cuuint64_t strides[2] = {t_out * eb, t_out * eb * co};
+  cuuint32_t box[3] = {32u * phases, 32u / phases, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return fn(map, dt, 3, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_out_map(CUtensorMap* map, void* out, int out_kind, int64_t M, int N) {
   const int eb = out_bytes(out_kind);
   const CUtensorMapDataType dt = out_kind == OUT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -134,6 +152,15 @@ constexpr int kFp4StatStages = 6;      // NVFP4: 6 x 18 KB of A (+ scales) + 72 
 bool streaming_forced() {
   static const bool forced = [] {
     const char* v = getenv("ISP_GEMM_STREAMING");
+    return v != nullptr && v[0] == '1';
+  }();
+  return forced;
+}
+
+// ISP_CONV_DIRECT_STORE=1 keeps the convolution epilogue on per-element stores.
+bool conv_direct_forced() {
+  static const bool forced = [] {
+    const char* v = getenv("ISP_CONV_DIRECT_STORE");
     return v != nullptr && v[0] == '1';
   }();
   return forced;
@@ -251,15 +278,16 @@ int dispatch_decode(int out_kind, const CUtensorMap& a, const CUtensorMap& b, co
   }
 }
 
-// Polyphase tap table of a convolution.  Conv1d (stride S): one phase; slot j is
-// tap j at input position t * S + o, o = j * dilation - padding, which in the A view
-// [rows / S, S * C_pad] is row t + floor(o / S), column block (o mod S) * C_pad / 128.
-// ConvTranspose1d (stride S): output time t = q * S + r gathers input q + (r + padding
-// - tap * dilation) / S from the taps with tap * dilation = r + padding (mod S); phase
-// r lists those taps (zero slots pad every phase to the same count).
+// Phase-folded form of a convolution: output time t = q * P + r is row q, column
+// co * P + r of one GEMM whose K runs over window slots j (128-channel blocks each).
+// Conv1d (stride S): P = 1, slot j is tap j at input position t * S + o,
+// o = j * dilation - padding, which in the A view [rows / S, S * C_pad] is row
+// t + floor(o / S), column block (o mod S) * C_pad / 128.
+// ConvTranspose1d (stride S): P = S; output q * S + r gathers input q + R from tap k
+// when r + padding - k * dilation = R * S; slot j covers R = r_min + j for every phase
+// at once (taps that do not reach a (phase, slot) pair are zero weights).
 struct ConvGeom {
-  int phases, taps, a_stride;
-  int tap[kConvTab];
+  int phases, taps, a_stride, r_min;
   int row[kConvTab];
   int colstep[kConvTab];
 };
@@ -276,49 +304,43 @@ int conv_geometry(int KW, int stride, int dilation, int padding, int transposed,
     g->phases = 1;
     g->taps = KW;
     g->a_stride = stride;
+    g->r_min = 0;
     for (int j = 0; j < KW; ++j) {
       const int64_t o = static_cast<int64_t>(j) * dilation - padding;
       const int64_t row = floor_div(o, stride);
-      g->tap[j] = j;
       g->row[j] = static_cast<int>(row);
       g->colstep[j] = static_cast<int>(o - row * stride);
     }
     return ISP_OK;
   }
-  g->phases = stride;
-  g->a_stride = 1;
-  int taps = 1;
-  for (int r = 0; r < stride; ++r) {
-    int n = 0;
-    for (int k = 0; k < KW; ++k)
-      if ((static_cast<int64_t>(r) + padding - static_cast<int64_t>(k) * dilation) % stride == 0) ++n;
-    taps = n > taps ? n : taps;
-  }
-  if (static_cast<int64_t>(stride) * taps > kConvTab) return ISP_ERR_SHAPE;
-  g->taps = taps;
-  for (int r = 0; r < stride; ++r) {
-    int n = 0;
+  int64_t lo = 0, hi = -1;
+  for (int r = 0; r < stride; ++r)
     for (int k = 0; k < KW; ++k) {
       const int64_t num = static_cast<int64_t>(r) + padding - static_cast<int64_t>(k) * dilation;
       if (num % stride != 0) continue;
-      g->tap[r * taps + n] = k;
-      g->row[r * taps + n] = static_cast<int>(floor_div(num, stride));
-      g->colstep[r * taps + n] = 0;
-      ++n;
+      const int64_t R = num / stride;
+      if (hi < lo) lo = hi = R;
+      lo = R < lo ? R : lo;
+      hi = R > hi ? R : hi;
     }
-    for (; n < taps; ++n) {
-      g->tap[r * taps + n] = -1;
-      g->row[r * taps + n] = 0;
-      g->colstep[r * taps + n] = 0;
-    }
+  if (hi < lo) lo = hi = 0;                    // no tap reaches any output: one zero slot
+  if (hi - lo + 1 > kConvTab) return ISP_ERR_SHAPE;
+  g->phases = stride;
+  g->taps = static_cast<int>(hi - lo + 1);
+  g->a_stride = 1;
+  g->r_min = static_cast<int>(lo);
+  for (int j = 0; j < g->taps; ++j) {
+    g->row[j] = static_cast<int>(lo) + j;
+    g->colstep[j] = 0;
   }
   return ISP_OK;
 }
 
 template <int kAB, int kOut>
-int launch_conv(bool stat, const CUtensorMap& a, const CUtensorMap& b, const Params& p, cudaStream_t s) {
-  return stat ? launch<kBN, kStatStages, kScaleEpiWarps, kAB, EPI_CONV, kOut, kStatK>(a, b, b, a, p, s)
-              : launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_CONV, kOut>(a, b, b, a, p, s);
+int launch_conv(bool stat, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const Params& p,
+                cudaStream_t s) {
+  return stat ? launch<kBN, kStatStages, kScaleEpiWarps, kAB, EPI_CONV, kOut, kStatK>(a, b, b, o, p, s)
+              : launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_CONV, kOut>(a, b, b, o, p, s);
 }
 
 int out_kind_of(int dtype) {
@@ -447,9 +469,13 @@ int isp_conv1d_pack_weight(const void* codes, int64_t ldw, int CO, int CI, int K
   p.phases = g.phases;
   p.taps = g.taps;
   p.c_pad = C_pad;
+  p.transposed = transposed ? 1 : 0;
+  p.stride = stride;
+  p.dilation = dilation;
+  p.padding = padding;
+  p.r_min = g.r_min;
   p.dst = static_cast<uint8_t*>(w_packed);
-  for (int i = 0; i < g.phases * g.taps; ++i) p.tap[i] = g.tap[i];
-  const int64_t total = static_cast<int64_t>(g.phases) * CO * g.taps * (C_pad / 16);
+  const int64_t total = static_cast<int64_t>(CO) * g.phases * g.taps * (C_pad / 16);
   isp::conv_pack_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(p);
   return isp::launch_status();
 }
@@ -532,49 +558,57 @@ int isp_conv1d(const void* xq, int ab_dtype, int64_t B, int C_pad, int64_t T_in,
   if (B == 0) return ISP_OK;
   const int64_t k_bytes = static_cast<int64_t>(g.taps) * C_pad;
   const int64_t t_rows = (T_in + g.a_stride - 1) / g.a_stride;   // rows of the A view per utterance
-  const int64_t q_rows = (T_out + g.phases - 1) / g.phases;      // output rows of phase 0
+  const int64_t q_rows = (T_out + g.phases - 1) / g.phases;      // phase rows per utterance
   const int tpb = static_cast<int>((q_rows + kBM - 1) / kBM);
-  const int ntco = (CO + kBN - 1) / kBN;
-  if (k_bytes > 0x7FFFFFFFll || static_cast<int64_t>(B) * tpb * kBM > 0x7FFFFFFFll ||
-      static_cast<int64_t>(B) * tpb * g.phases * ntco > 0x7FFFFFFFll)
+  const int64_t n_cols = static_cast<int64_t>(CO) * g.phases;
+  if (k_bytes > 0x7FFFFFFFll || n_cols > 0x7FFFFFFFll || static_cast<int64_t>(B) * tpb * kBM > 0x7FFFFFFFll ||
+      static_cast<int64_t>(B) * tpb * ((n_cols + kBN - 1) / kBN) > 0x7FFFFFFFll)
     return ISP_ERR_SHAPE;
   CUtensorMap ta, tb;
   if (!make_map3d_u8(&ta, xq, static_cast<uint64_t>(g.a_stride) * C_pad, static_cast<uint64_t>(t_rows),
                      static_cast<uint64_t>(B), kBK, kBM) ||
-      !make_map3d_u8(&tb, w_packed, static_cast<uint64_t>(k_bytes), static_cast<uint64_t>(CO),
-                     static_cast<uint64_t>(g.phases), kBK, kBN))
+      !make_map(&tb, w_packed, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, static_cast<uint64_t>(k_bytes),
+                static_cast<uint64_t>(n_cols), kBK, kBN))
     return ISP_ERR_ALIGN;
   Params p{};
   p.conv_tpb = tpb;
-  p.conv_ntco = ntco;
   p.conv_phases = g.phases;
   p.conv_taps = g.taps;
   p.conv_cblocks = cblocks;
+  p.conv_co = CO;
   p.conv_tout = T_out;
   p.conv_amax = amax;
-  for (int i = 0; i < g.phases * g.taps; ++i) p.conv_tab[i] = g.row[i] * 1024 + g.colstep[i] * cblocks;
+  for (int j = 0; j < g.taps; ++j) p.conv_tab[j] = g.row[j] * 1024 + g.colstep[j] * cblocks;
   p.M = static_cast<int>(B * tpb * kBM);
-  p.N = CO;
+  p.N = static_cast<int>(n_cols);
   p.K = static_cast<int>(k_bytes);
   p.m_tiles = static_cast<int>(B * tpb);
-  p.n_tiles = g.phases * ntco;
+  p.n_tiles = static_cast<int>((n_cols + kBN - 1) / kBN);
   p.k_blocks = g.taps * cblocks;
   p.a_scale = amax != nullptr ? 1.f : in_scale;   // dynamic: the epilogue applies the utterance's scale
   p.w_scale = w_scale;
   p.bias = bias;
   p.out = y;
+  // Output boxes through a tensor map where its rules allow (row pitch a multiple of
+  // 16 bytes, at most 8 phases); otherwise per-element stores.
+  const int out_kind = out_dtype == ISP_F32 ? OUT_F32 : (out_dtype == ISP_F16 ? OUT_F16 : OUT_BF16);
+  CUtensorMap to = ta;
+  p.conv_tma_store = (g.phases == 1 || g.phases == 2 || g.phases == 4 || g.phases == 8) &&
+                     (T_out * out_bytes(out_kind)) % 16 == 0 && !conv_direct_forced() &&
+                     make_conv_out_map(&to, y, out_kind, static_cast<uint64_t>(T_out), static_cast<uint64_t>(CO),
+                                       static_cast<uint64_t>(B), static_cast<uint32_t>(g.phases));
   const bool stat = k_bytes <= kStatK && !streaming_forced();
   if (ab_dtype == ISP_I8) {
     switch (out_dtype) {
-      case ISP_F32: return launch_conv<AB_I8, OUT_F32>(stat, ta, tb, p, stream);
-      case ISP_F16: return launch_conv<AB_I8, OUT_F16>(stat, ta, tb, p, stream);
-      default: return launch_conv<AB_I8, OUT_BF16>(stat, ta, tb, p, stream);
+      case ISP_F32: return launch_conv<AB_I8, OUT_F32>(stat, ta, tb, to, p, stream);
+      case ISP_F16: return launch_conv<AB_I8, OUT_F16>(stat, ta, tb, to, p, stream);
+      default: return launch_conv<AB_I8, OUT_BF16>(stat, ta, tb, to, p, stream);
     }
   }
   switch (out_dtype) {
-    case ISP_F32: return launch_conv<AB_E4M3, OUT_F32>(stat, ta, tb, p, stream);
-    case ISP_F16: return launch_conv<AB_E4M3, OUT_F16>(stat, ta, tb, p, stream);
-    default: return launch_conv<AB_E4M3, OUT_BF16>(stat, ta, tb, p, stream);
+    case ISP_F32: return launch_conv<AB_E4M3, OUT_F32>(stat, ta, tb, to, p, stream);
+    case ISP_F16: return launch_conv<AB_E4M3, OUT_F16>(stat, ta, tb, to, p, stream);
+    default: return launch_conv<AB_E4M3, OUT_BF16>(stat, ta, tb, to, p, stream);
   }
 }
 

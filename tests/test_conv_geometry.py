@@ -1,5 +1,5 @@
 """CPU checks of the implicit-conv geometry (host code of the C ABI, no GPU):
-the polyphase tap table covers exactly the reference's gather positions, and
+the phase-folded window covers exactly the reference's gather positions, and
 bad geometries are rejected before any device work."""
 import ctypes
 
@@ -16,47 +16,55 @@ def lib():
     return _lib.load()
 
 
-def phase_taps(kw, stride, dilation, padding, transpose):
-    """Restatement: Conv1d is one phase of all taps; ConvTranspose1d phase r
-    holds the taps with (r + padding - tap * dilation) divisible by stride."""
+def folded_window(kw, stride, dilation, padding, transpose):
+    """Restatement: Conv1d is one phase over all taps; ConvTranspose1d folds the
+    stride's phases into columns and spans the input offsets R = (r + padding -
+    k * dilation) / stride that any (phase r, tap k) pair reads."""
     if not transpose:
-        return 1, kw
-    counts = [sum((r + padding - k * dilation) % stride == 0 for k in range(kw)) for r in range(stride)]
-    return stride, max(1, max(counts))
+        return 1, kw, 0
+    offsets = [(r + padding - k * dilation) // stride for r in range(stride) for k in range(kw)
+               if (r + padding - k * dilation) % stride == 0]
+    if not offsets:
+        return stride, 1, 0
+    return stride, max(offsets) - min(offsets) + 1, min(offsets)
 
 
 GEOMS = [(3, 1, 5, 5, False), (7, 1, 1, 3, False), (4, 2, 1, 1, False), (16, 8, 1, 4, True), (3, 2, 2, 1, True),
-         (5, 3, 1, 1, True), (12, 6, 1, 3, True), (11, 5, 1, 3, True), (4, 4, 2, 0, True), (1, 1, 1, 0, False)]
+         (5, 3, 1, 1, True), (12, 6, 1, 3, True), (11, 5, 1, 3, True), (4, 4, 2, 0, True), (1, 1, 1, 0, False),
+         (8, 4, 1, 2, True), (7, 3, 2, 0, True)]
 
 
 @pytest.mark.parametrize("g", GEOMS)
 def test_geometry_matches_restatement(lib, g):
     phases, taps = ctypes.c_int(), ctypes.c_int()
     assert lib.isp_conv1d_geometry(*g[:4], int(g[4]), ctypes.byref(phases), ctypes.byref(taps)) == 0
-    assert (phases.value, taps.value) == phase_taps(*g)
+    assert (phases.value, taps.value) == folded_window(*g)[:2]
 
 
 @pytest.mark.parametrize("g", [g for g in GEOMS if g[4]])
-def test_polyphase_taps_cover_every_gather_position(g):
-    """Every (output time, tap) pair that ``ops/triton/fp8_conv.py:31-33`` reads
-    lands in exactly one phase slot with the same input index."""
+def test_folded_window_covers_every_gather_position(g):
+    """Every (output time, tap, input row) triple that ``ops/triton/fp8_conv.py:
+    31-33`` reads is formed exactly once by some (phase, window slot) of the
+    folded GEMM, with the tap the weight packing assigns to that pair."""
     kw, s, dil, pad, _ = g
+    _, slots, r_min = folded_window(*g)
     t_out = 64
-    seen = set()
+    seen = []
     for r in range(s):
-        for k in range(kw):
-            num = r + pad - k * dil
-            if num % s:
-                continue
+        for j in range(slots):
+            num = r + pad - (r_min + j) * s
+            if num < 0 or num % dil or num // dil >= kw:
+                continue                       # zero weight in this (phase, slot)
+            k = num // dil
             for q in range((t_out - r + s - 1) // s):
-                seen.add((q * s + r, k, q + num // s))
+                seen.append((q * s + r, k, q + r_min + j))
     expected = set()
     for t in range(t_out):
         for k in range(kw):
             num = t + pad - k * dil
             if num % s == 0:
                 expected.add((t, k, num // s))
-    assert seen == expected
+    assert len(seen) == len(set(seen)) and set(seen) == expected
 
 
 def test_geometry_limits_and_host_validation(lib):

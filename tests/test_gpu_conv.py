@@ -1,4 +1,4 @@
-"""GPU parity: quantized learned Conv1d / ConvTranspose1d as the polyphase
+"""GPU parity: quantized learned Conv1d / ConvTranspose1d as the phase-folded
 implicit GEMM on tcgen05, against the oracle and the reference fixtures
 (``ops/triton/fp8_conv.conv1d`` through Triton's interpreter; ``ExportWeightOp``
 conv roles)."""
@@ -59,9 +59,12 @@ def test_matrix_conv_matches_triton_reference_fixture(C, name):
 GEOMETRIES = [
     (False, 128, 128, 3, 1, 5, 5, 0, 2, 700),        # BigVGAN resblock conv (dilation 5), stationary B
     (False, 512, 256, 7, 1, 3, 1, 0, 2, 300),        # conv_pre-like, streaming B (K = 3584)
-    (True, 256, 128, 16, 8, 4, 1, 0, 2, 90),         # upsampling ConvTranspose1d, 8 phases x 2 taps
+    (True, 256, 128, 16, 8, 4, 1, 0, 2, 90),         # upsampling ConvTranspose1d, 8 phases, window 3
     (True, 200, 40, 5, 3, 1, 1, 2, 3, 61),           # ragged phases, C and CO unaligned, output_padding
+    (True, 200, 40, 5, 3, 1, 1, 1, 3, 61),           # the same through the strided TMA store (T_out = 184)
     (False, 96, 72, 4, 2, 1, 1, 0, 3, 259),          # strided Conv1d (A view of 2 x C_pad columns)
+    (True, 64, 48, 4, 2, 1, 1, 0, 2, 512),           # ConvTranspose1d stride 2 through the TMA store
+    (True, 128, 80, 7, 3, 0, 2, 0, 2, 100),          # dilated ConvTranspose1d, non-power-of-2 stride
     (False, 64, 300, 1, 1, 0, 1, 0, 1, 1000),        # pointwise, two channel tiles
 ]
 
@@ -89,8 +92,13 @@ def test_matrix_conv_bf16_and_f16_inputs(C):
     g = np.random.default_rng(7)
     w = (g.standard_normal((co, ci, kw)) * 0.05).astype(np.float32)
     packed, scales = og.pack_weight(w.reshape(co, ci * kw))
-    x = bf16_round(g.standard_normal((2, ci, 333)).astype(np.float32))
-    ref32 = oconv.matrix_conv1d(x, packed, scales, None, ci, co, kw, s, pad, dil, tr)
+    for t in (333, 336):                             # per-element and tensor-map output stores
+        x = bf16_round(g.standard_normal((2, ci, t)).astype(np.float32))
+        ref32 = oconv.matrix_conv1d(x, packed, scales, None, ci, co, kw, s, pad, dil, tr)
+        _check_half_outputs(C, x, packed, scales, ref32, ci, co, kw, s, pad, dil, tr)
+
+
+def _check_half_outputs(C, x, packed, scales, ref32, ci, co, kw, s, pad, dil, tr):
     for dt in (torch.bfloat16, torch.float16):
         y = C.conv1d(torch.from_numpy(x).cuda().to(dt), packed_dev(packed), torch.from_numpy(scales).cuda(), None, ci,
                      co, kw, s, pad, dil, tr, 0)
@@ -160,7 +168,7 @@ def test_export_int8_smoothquant_conv_vs_oracle(C):
 
 
 def test_export_deconv_static_vs_zero_insertion_oracle(C):
-    """The polyphase ConvTranspose1d equals the reference's zero-insertion
+    """The phase-folded ConvTranspose1d equals the reference's zero-insertion
     rewrite (same code products), including output_padding."""
     ci, co, kw, s, pad, op = 128, 96, 12, 6, 3, 2
     g = np.random.default_rng(5)
@@ -188,5 +196,5 @@ def test_fp8_matrix_conv_module(C):
     ref = oconv.matrix_conv1d(x.cpu().numpy(), packed, m.scales.cpu().numpy(), m.bias.detach().cpu().numpy(), 64, 32,
                               4, 2, 1, 1, True)
     assert rel_l2(y.detach().cpu().numpy(), ref) < 1e-5
-    # two calls in a row reuse the cached polyphase weight
+    # two calls in a row reuse the cached folded weight
     assert torch.equal(m(x), y)
