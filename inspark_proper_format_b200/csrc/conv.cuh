@@ -26,13 +26,37 @@ namespace isp {
 template <bool kBf16>
 __global__ void __launch_bounds__(256) conv_amax_kernel(const void* x, int64_t per_utt, float* amax) {
   const int64_t base = static_cast<int64_t>(blockIdx.y) * per_utt;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   float m = 0.f;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < per_utt;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float v;
-    if constexpr (kBf16) v = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[base + i]);
-    else v = __ldg(static_cast<const float*>(x) + base + i);
-    m = fmaxf(m, fabsf(v));
+  if constexpr (kBf16) {
+    const __nv_bfloat16* xs = static_cast<const __nv_bfloat16*>(x) + base;
+    // 16-byte loads (8 values) when the utterance starts 16-byte aligned
+    if ((reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
+      const int64_t n8 = per_utt / 8;
+      for (int64_t i = first; i < n8; i += stride) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(xs) + i);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[j] << 16)),
+                                                       fabsf(__uint_as_float(w[j] & 0xFFFF0000u))));
+      }
+      for (int64_t i = n8 * 8 + first; i < per_utt; i += stride) m = fmaxf(m, fabsf(__bfloat162float(xs[i])));
+    } else {
+      for (int64_t i = first; i < per_utt; i += stride) m = fmaxf(m, fabsf(__bfloat162float(xs[i])));
+    }
+  } else {
+    const float* xs = static_cast<const float*>(x) + base;
+    if ((reinterpret_cast<uintptr_t>(xs) & 15) == 0) {
+      const int64_t n4 = per_utt / 4;
+      for (int64_t i = first; i < n4; i += stride) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(xs) + i);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w))));
+      }
+      for (int64_t i = n4 * 4 + first; i < per_utt; i += stride) m = fmaxf(m, fabsf(__ldg(xs + i)));
+    } else {
+      for (int64_t i = first; i < per_utt; i += stride) m = fmaxf(m, fabsf(__ldg(xs + i)));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -53,7 +77,6 @@ struct ConvQuantParams {
   int64_t T;
   int64_t t_rows;          // rows written per utterance (>= T; rows >= T are zero)
   int c_pad;
-  int chunks;              // c_pad / 16
   float scale;             // static input scale (amax == nullptr)
   float rscale;            // RN(1 / scale)
   const float* amax;       // dynamic: per-utterance max |x|, scale = max(amax / 448, 1e-12)
@@ -61,43 +84,77 @@ struct ConvQuantParams {
   uint8_t* xq;             // [B, t_rows, c_pad]
 };
 
-// One thread per (row, 16 channels); lanes take consecutive rows, so every
-// per-channel read of x is one contiguous row segment.
+// A block transposes one tile of 64 rows x 128 channels through shared memory:
+// loads walk time (a warp reads 32 consecutive samples of one channel, 128 bytes),
+// each thread codes 4 channels of one row into a word at [row][channel / 4] (row
+// pitch 33 words: conflict-free), and stores walk channels (a warp writes one
+// 128-byte channels-last row).  grid (ceil(t_rows / 64), c_pad / 128, B).
+constexpr int kCqRows = 64;
+constexpr int kCqPitch = 33;                 // words per staged row (32 + 1 pad)
+
+template <bool kBf16>
+ISP_D float conv_load(const void* x, int64_t off) {
+  if constexpr (kBf16) return __bfloat162float(static_cast<const __nv_bfloat16*>(x)[off]);
+  else return __ldg(static_cast<const float*>(x) + off);
+}
+
 template <bool kInt8, bool kBf16>
 __global__ void __launch_bounds__(256) conv_quant_kernel(ConvQuantParams p) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = p.B * p.chunks * p.t_rows;
-  if (i >= total) return;
-  const int64_t t = i % p.t_rows;
-  const int64_t rest = i / p.t_rows;
-  const int chunk = static_cast<int>(rest % p.chunks);
-  const int64_t b = rest / p.chunks;
+  __shared__ uint32_t tile[kCqRows * kCqPitch];
+  const int64_t b = blockIdx.z;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kCqRows;
+  const int c0 = blockIdx.y * 128;
   float scale = p.scale, rscale = p.rscale;
   if (p.amax != nullptr) {
     scale = gemm::conv_dynamic_scale(__ldg(p.amax + b));
     rscale = __frcp_rn(scale);
   }
-  uint32_t w[4] = {0u, 0u, 0u, 0u};
+  // thread -> row r (fixed) and channel groups quad0 + 4i; the block's first element
+  const int r = threadIdx.x % kCqRows;
+  const int quad0 = threadIdx.x / kCqRows;
+  const int64_t t = t0 + r;
+  const int64_t base = (b * p.C + c0) * p.T + t;
+  const bool interior = t0 + kCqRows <= p.T && c0 + 128 <= p.C;   // block-uniform
+#pragma unroll 2
+  for (int i = 0; i < 8; ++i) {
+    const int quad = quad0 + 4 * i;
+    const int64_t off = base + static_cast<int64_t>(quad * 4) * p.T;
+    float v[4];
+    if (interior) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int c = chunk * 16 + j;
-    float v = 0.f;
-    if (t < p.T && c < p.C) {
-      const int64_t off = (b * p.C + c) * p.T + t;
-      if constexpr (kBf16) v = __bfloat162float(static_cast<const __nv_bfloat16*>(p.x)[off]);
-      else v = __ldg(static_cast<const float*>(p.x) + off);
+      for (int j = 0; j < 4; ++j) v[j] = conv_load<kBf16>(p.x, off + j * p.T);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        v[j] = (t < p.T && c0 + quad * 4 + j < p.C) ? conv_load<kBf16>(p.x, off + j * p.T) : 0.f;
     }
-    uint32_t code;
+    uint32_t word;
     if constexpr (kInt8) {
-      if (p.smooth != nullptr && c < p.C) v = __fdiv_rn(v, __ldg(p.smooth + c));
-      code = static_cast<uint8_t>(int8_rne_sat(div_rn_recip(v, scale, rscale)));
+      word = 0u;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = c0 + quad * 4 + j;
+        float u = v[j];
+        if (p.smooth != nullptr && c < p.C) u = __fdiv_rn(u, __ldg(p.smooth + c));
+        word |= static_cast<uint32_t>(static_cast<uint8_t>(int8_rne_sat(div_rn_recip(u, scale, rscale)))) << (8 * j);
+      }
     } else {
       // satfinite == the reference's clamp(-448, 448) before the cast
-      code = e4m3x2(div_rn_recip(v, scale, rscale), 0.f) & 0xFFu;
+      word = static_cast<uint32_t>(e4m3x2(div_rn_recip(v[0], scale, rscale), div_rn_recip(v[1], scale, rscale))) |
+             static_cast<uint32_t>(e4m3x2(div_rn_recip(v[2], scale, rscale), div_rn_recip(v[3], scale, rscale)))
+                 << 16;
     }
-    w[j >> 2] |= code << (8 * (j & 3));
+    tile[r * kCqPitch + quad] = word;
   }
-  *reinterpret_cast<uint4*>(p.xq + (b * p.t_rows + t) * p.c_pad + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+  __syncthreads();
+#pragma unroll 2
+  for (int k = threadIdx.x; k < kCqRows * 32; k += 256) {
+    const int rr = k / 32;
+    const int w = k % 32;
+    const int64_t tt = t0 + rr;
+    if (tt < p.t_rows)
+      reinterpret_cast<uint32_t*>(p.xq + (b * p.t_rows + tt) * p.c_pad + c0)[w] = tile[rr * kCqPitch + w];
+  }
 }
 
 // ---- weight packing ----------------------------------------------------------

@@ -488,7 +488,8 @@ int isp_conv1d_quant(const void* x, int x_dtype, int64_t B, int C, int64_t T, in
   if (smooth != nullptr && code_dtype != ISP_I8) return ISP_ERR_ARG;
   if (amax != nullptr && (code_dtype != ISP_E4M3 || in_scale != 0.f)) return ISP_ERR_ARG;
   if (amax == nullptr && !isp::gemm::global_scale_ok(in_scale)) return ISP_ERR_ARG;
-  if (B < 0 || C <= 0 || T <= 0 || row_multiple < 1 || C_pad < C || C_pad % 128 != 0) return ISP_ERR_SHAPE;
+  if (B < 0 || B > 65535 || C <= 0 || T <= 0 || row_multiple < 1 || C_pad < C || C_pad % 128 != 0)
+    return ISP_ERR_SHAPE;
   if (!isp::aligned16(xq)) return ISP_ERR_ALIGN;
   if (int st = isp::check_device()) return st;
   if (B == 0) return ISP_OK;
@@ -496,10 +497,10 @@ int isp_conv1d_quant(const void* x, int x_dtype, int64_t B, int C, int64_t T, in
     if (cudaMemsetAsync(amax, 0, static_cast<size_t>(B) * sizeof(float), stream) != cudaSuccess)
       return ISP_ERR_LAUNCH;
     const int64_t per = static_cast<int64_t>(C) * T;
-    const int64_t want = (per + 256 * 16 - 1) / (256 * 16);         // >= 16 elements per thread
-    const unsigned bx = static_cast<unsigned>(want < 1024 ? want : 1024);
+    const int64_t want = (per + 256 * 32 - 1) / (256 * 32);         // >= 32 elements per thread
+    const int64_t cap = (4 * isp::sm_count() + B - 1) / B;     // ~4 blocks per SM over all utterances
+    const unsigned bx = static_cast<unsigned>(want < cap ? (want > 0 ? want : 1) : cap);
     const dim3 grid(bx, static_cast<unsigned>(B));
-    if (B > 65535) return ISP_ERR_SHAPE;
     if (x_dtype == ISP_BF16) isp::conv_amax_kernel<true><<<grid, 256, 0, stream>>>(x, per, amax);
     else isp::conv_amax_kernel<false><<<grid, 256, 0, stream>>>(x, per, amax);
   }
@@ -510,15 +511,14 @@ int isp_conv1d_quant(const void* x, int x_dtype, int64_t B, int C, int64_t T, in
   p.T = T;
   p.t_rows = (T + row_multiple - 1) / row_multiple * row_multiple;
   p.c_pad = C_pad;
-  p.chunks = C_pad / 16;
   // RN(1/s): the host division is IEEE single precision, the reciprocal the kernels expect
   p.scale = amax != nullptr ? 1.f : in_scale;
   p.rscale = 1.f / p.scale;
   p.amax = amax;
   p.smooth = smooth;
   p.xq = static_cast<uint8_t*>(xq);
-  const int64_t total = B * p.chunks * p.t_rows;
-  const unsigned grid = static_cast<unsigned>((total + 255) / 256);
+  const dim3 grid(static_cast<unsigned>((p.t_rows + isp::kCqRows - 1) / isp::kCqRows), static_cast<unsigned>(C_pad / 128),
+                  static_cast<unsigned>(B));
   const bool bf16 = x_dtype == ISP_BF16;
   if (code_dtype == ISP_I8) {
     if (bf16) isp::conv_quant_kernel<true, true><<<grid, 256, 0, stream>>>(p);
