@@ -76,16 +76,17 @@ ISP_D uint32_t e2m1x2(float lo, float hi) {
 // correction (P. Markstein, IBM J. Res. Dev. 34(1), 1990; Muller et al.,
 // "Handbook of Floating-Point Arithmetic", ch. 4): q = RN(x y), the residual
 // r = x - q d is exact in one FMA, and RN(q + r y) is the correctly rounded
-// quotient.  The correction is applied twice.  Exact for normal d below
-// 2^126; when the first product is out of range (|q| >= 2^100, inf, NaN) or
-// d is zero or at least 2^126, x * y is returned, which equals x / d up to the
-// saturation every caller applies next (inf, NaN and 0 propagate as in x / d).
+// quotient when y is the correctly rounded reciprocal and q is within one ulp
+// (Markstein's theorem; one correction step).  Exact for normal d below 2^126
+// and normal quotients (a subnormal quotient can differ by one subnormal ulp,
+// below every code's resolution); when the first product is out of range
+// (|q| >= 2^100, inf, NaN) or d is zero or at least 2^126, x * y is returned,
+// which equals x / d up to the saturation every caller applies next (inf, NaN
+// and 0 propagate as in x / d).
 ISP_D float div_rn_recip(float x, float d, float y) {
   const float q0 = __fmul_rn(x, y);
-  float r = __fmaf_rn(-q0, d, x);
-  float q = __fmaf_rn(r, y, q0);
-  r = __fmaf_rn(-q, d, x);
-  q = __fmaf_rn(r, y, q);
+  const float r = __fmaf_rn(-q0, d, x);
+  const float q = __fmaf_rn(r, y, q0);
   return (fabsf(q0) < 0x1p100f && fabsf(d) < 0x1p126f) ? q : q0;
 }
 
@@ -96,6 +97,12 @@ ISP_D int8_t int8_rne_sat(float v) {
 }
 
 ISP_D float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// RN to BF16 of (lo, hi) in one conversion: lo in bits 0-15, hi in bits 16-31.
+ISP_D uint32_t pack_bf16_rn(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
 
 // ---------------------------------------------------------------------------
 // Global-memory vector helpers

@@ -1,8 +1,10 @@
-// Fused row normalization -> quantization (memory-bound, one warp per row).
+// Fused row normalization -> quantization (memory-bound; kLanes = 16 or 32 lanes
+// per row, i.e. two rows or one row per warp).
 //
-// Each lane owns groups of 8 consecutive elements (group g = lane + 32 i), so
-// a warp streams 256 contiguous elements per step with 16-byte loads (BF16) or
-// two 16-byte loads (FP32).  The row statistic is accumulated in double from
+// Each lane owns groups of 8 consecutive elements (group g = sublane + kLanes i),
+// so a row's lanes stream 8 kLanes contiguous elements per step with 16-byte loads
+// (BF16) or two 16-byte loads (FP32).  Half-warp rows (K <= 512) give every lane
+// twice the elements over which to spread the per-row reduction and scalar math.  The row statistic is accumulated in double from
 // FP32 squares and rounded once; every following step is one IEEE FP32
 // operation in the order of the reference module (see isp_b200.h for the
 // reference file:line of each mode).
@@ -52,41 +54,51 @@ ISP_D void load_group(const void* row, int g, float (&v)[8]) {
   }
 }
 
-ISP_D double warp_sum(double v) {
+// Reductions over the kLanes lanes of a row (xor offsets stay inside the row).
+template <int kLanes>
+ISP_D double row_sum(double v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  for (int o = kLanes / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
-ISP_D float warp_max(float v) {
+template <int kLanes>
+ISP_D float row_max(float v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  for (int o = kLanes / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
 
-// kGroups: max 8-element groups per lane kept in registers (K <= 256 * kGroups).
-template <bool kBF16, int kNorm, int kFmt, int kGroups>
+// kGroups: max 8-element groups per lane kept in registers (K <= 8 * kLanes * kGroups).
+// A block of 8 warps covers 8 * 32 / kLanes rows; rows past M keep their lanes in
+// the shuffles and skip every load and store.
+template <bool kBF16, int kNorm, int kFmt, int kGroups, int kLanes>
 __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= p.M) return;
+  static_assert(kLanes == 16 || kLanes == 32, "a row spans a half or a whole warp");
+  const int lane = threadIdx.x % kLanes;   // lane within the row
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * (32 / kLanes) +
+                      (threadIdx.x & 31) / kLanes;
+  const bool active = row < p.M;
+  if (__all_sync(0xffffffffu, !active)) return;
   const int K = p.K;
-  const int ngroups = K >> 3;
+  const int ngroups = active ? K >> 3 : 0;   // an inactive row owns no groups
   const void* xrow = kBF16 ? static_cast<const void*>(static_cast<const uint16_t*>(p.x) + row * K)
                            : static_cast<const void*>(static_cast<const float*>(p.x) + row * K);
 
   float v[kGroups][8];
 #pragma unroll
   for (int i = 0; i < kGroups; ++i) {
-    const int g = lane + 32 * i;
+    const int g = lane + kLanes * i;
     if (g < ngroups) load_group<kBF16>(xrow, g, v[i]);
   }
 
   // ---- normalization ------------------------------------------------------
   if constexpr (kNorm != ISP_NORM_NONE) {
-    double ss = 0.0;
+    // four independent double accumulators (no serial add chain); the FP32 squares
+    // are summed exactly in double whatever the order, then rounded once
+    double acc[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
     for (int i = 0; i < kGroups; ++i) {
-      const int g = lane + 32 * i;
+      const int g = lane + kLanes * i;
       if (g < ngroups) {
         float b8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if constexpr (kNorm == ISP_NORM_BIAS) load_param8(p.bias, g, b8);
@@ -94,11 +106,11 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
         for (int j = 0; j < 8; ++j) {
           float d = v[i][j];
           if constexpr (kNorm == ISP_NORM_BIAS) d = __fsub_rn(d, b8[j]);
-          ss += static_cast<double>(__fmul_rn(d, d));
+          acc[j & 3] += static_cast<double>(__fmul_rn(d, d));
         }
       }
     }
-    ss = warp_sum(ss);
+    double ss = row_sum<kLanes>((acc[0] + acc[1]) + (acc[2] + acc[3]));
     const float mean = __fdiv_rn(static_cast<float>(ss), static_cast<float>(K));
     float r;
     if constexpr (kNorm == ISP_NORM_BIAS) {
@@ -108,7 +120,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
     }
 #pragma unroll
     for (int i = 0; i < kGroups; ++i) {
-      const int g = lane + 32 * i;
+      const int g = lane + kLanes * i;
       if (g < ngroups) {
         float gm[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
         if constexpr (kNorm == ISP_NORM_RMS_GPTFAST || kNorm == ISP_NORM_RMS_QWEN) load_param8(p.gamma, g, gm);
@@ -118,17 +130,28 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
           load_param8(p.ada_w + grp * K, g, aw);
           load_param8(p.ada_b + grp * K, g, ab);
         }
+        if constexpr (kNorm == ISP_NORM_RMS_GPTFAST && kBF16) {
+          // BF16 rounding of the normalized pair in one conversion
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            const uint32_t h = pack_bf16_rn(__fmul_rn(v[i][j], r), __fmul_rn(v[i][j + 1], r));
+            v[i][j] = __uint_as_float(h << 16);
+            v[i][j + 1] = __uint_as_float(h & 0xFFFF0000u);
+          }
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          float y = __fmul_rn(v[i][j], r);
+          float y = v[i][j];
           if constexpr (kNorm == ISP_NORM_RMS_GPTFAST) {
-            if constexpr (kBF16) y = bf16_round(y);
+            if constexpr (!kBF16) y = __fmul_rn(y, r);   // (BF16: normalized and rounded above)
             y = __fmul_rn(y, gm[j]);
             if (p.ada_w != nullptr) y = __fadd_rn(__fmul_rn(aw[j], y), ab[j]);
           } else if constexpr (kNorm == ISP_NORM_RMS_QWEN) {
+            y = __fmul_rn(y, r);
             y = __fmul_rn(y, gm[j]);
             if constexpr (kBF16) y = bf16_round(y);
           } else {
+            y = __fmul_rn(y, r);
             if constexpr (kBF16) y = bf16_round(y);
           }
           v[i][j] = y;
@@ -144,18 +167,18 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
       float amax = 0.f;
 #pragma unroll
       for (int i = 0; i < kGroups; ++i)
-        if (lane + 32 * i < ngroups)
+        if (lane + kLanes * i < ngroups)
 #pragma unroll
           for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
-      amax = warp_max(amax);
+      amax = row_max<kLanes>(amax);
       s = fmaxf(__fdiv_rn(amax, 448.f), 1e-12f);
-      if (lane == 0) static_cast<float*>(p.scales_out)[row] = s;
+      if (lane == 0 && active) static_cast<float*>(p.scales_out)[row] = s;
     }
     uint8_t* out = static_cast<uint8_t*>(p.codes) + row * K;
     const float rs = __frcp_rn(s);
 #pragma unroll
     for (int i = 0; i < kGroups; ++i) {
-      const int g = lane + 32 * i;
+      const int g = lane + kLanes * i;
       if (g < ngroups) {
         uint32_t w[2];
 #pragma unroll
@@ -174,7 +197,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
     const float rscale = __frcp_rn(p.scale);
 #pragma unroll
     for (int i = 0; i < kGroups; ++i) {
-      const int g = lane + 32 * i;
+      const int g = lane + kLanes * i;
       if (g < ngroups) {
         uint32_t w[2] = {0u, 0u};
         float sm[8];
@@ -202,7 +225,7 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
     const float six_g = __fmul_rn(6.f, gscale);
 #pragma unroll
     for (int i = 0; i < kGroups; ++i) {
-      const int g = lane + 32 * i;
+      const int g = lane + kLanes * i;
       // Every lane runs the shuffle; lanes without a group contribute 0.
       float amax = 0.f;
       if (g < ngroups)
@@ -232,14 +255,20 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
 
 template <bool kBF16, int kNorm, int kFmt>
 int launch_norm_quant_groups(const NormQuantParams& p, cudaStream_t stream) {
+  const dim3 block(256);
+  if (p.K <= 512) {   // half-warp rows: 16 rows per block, up to 4 groups per lane
+    const dim3 grid(static_cast<unsigned>((p.M + 15) / 16));
+    if (p.K <= 256) norm_quant_kernel<kBF16, kNorm, kFmt, 2, 16><<<grid, block, 0, stream>>>(p);
+    else norm_quant_kernel<kBF16, kNorm, kFmt, 4, 16><<<grid, block, 0, stream>>>(p);
+    return launch_status();
+  }
   const int per_lane = (p.K / 8 + 31) / 32;
-  const dim3 grid(static_cast<unsigned>((p.M + 7) / 8)), block(256);
-  if (per_lane <= 2) norm_quant_kernel<kBF16, kNorm, kFmt, 2><<<grid, block, 0, stream>>>(p);
-  else if (per_lane <= 4) norm_quant_kernel<kBF16, kNorm, kFmt, 4><<<grid, block, 0, stream>>>(p);
-  else if (per_lane <= 8) norm_quant_kernel<kBF16, kNorm, kFmt, 8><<<grid, block, 0, stream>>>(p);
-  else if (per_lane <= 16) norm_quant_kernel<kBF16, kNorm, kFmt, 16><<<grid, block, 0, stream>>>(p);
+  const dim3 grid(static_cast<unsigned>((p.M + 7) / 8));
+  if (per_lane <= 4) norm_quant_kernel<kBF16, kNorm, kFmt, 4, 32><<<grid, block, 0, stream>>>(p);
+  else if (per_lane <= 8) norm_quant_kernel<kBF16, kNorm, kFmt, 8, 32><<<grid, block, 0, stream>>>(p);
+  else if (per_lane <= 16) norm_quant_kernel<kBF16, kNorm, kFmt, 16, 32><<<grid, block, 0, stream>>>(p);
   else if constexpr (kNorm == ISP_NORM_NONE) {
-    if (per_lane <= 32) norm_quant_kernel<kBF16, kNorm, kFmt, 32><<<grid, block, 0, stream>>>(p);
+    if (per_lane <= 32) norm_quant_kernel<kBF16, kNorm, kFmt, 32, 32><<<grid, block, 0, stream>>>(p);
     else return ISP_ERR_SHAPE;
   } else {
     return ISP_ERR_SHAPE;

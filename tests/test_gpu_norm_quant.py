@@ -161,3 +161,39 @@ def test_adaln_bit_exact(nq, fmt, b, t, k):
         rp, rs = onq.quant_nvfp4(y, gs)
         np.testing.assert_array_equal(codes.cpu().numpy(), rp)
         np.testing.assert_array_equal(sf.view(torch.uint8).cpu().numpy(), rs)
+
+
+def _near_tie_inputs(m, k, s, grid_values, seed):
+    """FP32 x = RN(v * s) for values v at or next to the rounding boundaries of the
+    code grid, plus 1-ulp neighbours, so x / s lands within an FP32 ulp of a tie:
+    the cases where a quotient off by one ulp would change the code."""
+    g = np.random.default_rng(seed)
+    v = g.choice(grid_values, size=(m, k)).astype(np.float64)
+    x = (v * np.float64(s)).astype(np.float32)
+    step = g.integers(-2, 3, size=(m, k)).astype(np.int32)
+    x = (x.view(np.int32) + step).view(np.float32)          # walk up to 2 ulps either way
+    return x
+
+
+@pytest.mark.parametrize("k", [512, 1280])
+def test_quotient_rounding_at_e4m3_ties(nq, k):
+    """E4M3 codes of x / s where x / s sits on or beside E4M3 midpoints (5
+    significant bits) across the normal and subnormal E4M3 ranges: bit-exact."""
+    mids = np.array([(2 * m + 1) / 2 * 2.0 ** e for m in range(8, 16) for e in range(-9, 6)] +
+                    [(2 * m + 1) / 2 * 2.0 ** -9 for m in range(0, 8)], np.float64)
+    grid = np.concatenate([mids, -mids])
+    for seed, s in enumerate((0.0137, 3.0e-3, 0.71, 1.7e-5)):
+        x = _near_tie_inputs(64, k, s, grid, seed)
+        codes, _ = nq(torch.from_numpy(x).cuda(), kind="none", fmt="e4m3", scale=s)
+        ref = onq.quant_e4m3_static(x, s)
+        np.testing.assert_array_equal(codes.view(torch.uint8).cpu().numpy(), ref)
+
+
+def test_quotient_rounding_at_int8_ties(nq):
+    """INT8 codes of x / s with x / s on or beside k + 1/2: bit-exact."""
+    grid = np.array([k + 0.5 for k in range(-130, 130)], np.float64)
+    for seed, s in enumerate((0.0137, 3.1e-3, 1.3)):
+        x = _near_tie_inputs(64, 512, s, grid, seed + 10)
+        codes, _ = nq(torch.from_numpy(x).cuda(), kind="none", fmt="int8", scale=s)
+        ref = onq.quant_int8_static(x, s, None)
+        np.testing.assert_array_equal(codes.view(torch.int8).cpu().numpy(), ref)
