@@ -315,6 +315,30 @@ int isp_nvfp4_gated_up(const void *A, const void *A_sf, const void *W13, const v
                        int64_t M, int N, int K, float alpha_gate, float alpha_up, float h_scale,
                        void *h_codes, void *h_sf, isp_stream_t stream);
 
+/*
+ * No reference counterpart: an addition of this library for callers that cannot
+ * allocate device memory at call time -- an inference-engine plugin whose enqueue
+ * receives only pre-sized buffers, or a streaming audio worker that keeps the
+ * allocator (and its locks) off its per-chunk path.
+ *
+ * The dynamic-scale FP8 convolution (isp_conv1d_quant with amax != NULL, then
+ * isp_conv1d) in one call, with the per-utterance maxima kept in a static device
+ * array inside the library instead of a caller buffer.  xq is still the caller's
+ * [B, T_rows, C_pad] code buffer (sized as for isp_conv1d_quant); every other
+ * argument as isp_conv1d.
+ *   - B <= 8192 (ISP_ERR_SHAPE beyond); the call allocates nothing.
+ *   - The first call on each device resolves the array's address on that device
+ *     (device must be current); make that first call before any stream capture.
+ *   - The maxima are cleared at the start of each call.  One array per process and
+ *     device: calls that overlap in time (other streams, other threads) race on it
+ *     and must be serialized by the caller.
+ */
+int isp_conv1d_dynamic_noalloc(const void *x, int x_dtype, int64_t B, int C, int64_t T, void *xq,
+                               int C_pad, const void *w_packed, int CO, int KW, int stride,
+                               int dilation, int padding, int output_padding, int transposed,
+                               int64_t T_out, const float *w_scale, const float *bias, void *y,
+                               int out_dtype, isp_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -33,6 +33,8 @@ SIGNATURES = {
     "isp_conv1d_quant": (_i, [_vp, _i, _i64, _i, _i64, _i, _vp, _f, _vp, _i, _vp, _i, _vp]),
     "isp_conv1d": (_i, [_vp, _i, _i64, _i, _i64, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _f, _vp, _vp, _vp, _vp,
                         _i, _vp]),
+    "isp_conv1d_dynamic_noalloc": (_i, [_vp, _i, _i64, _i, _i64, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _i, _i64,
+                                        _vp, _vp, _vp, _i, _vp]),
     "isp_fir_snake": (_i, [_vp, _i64, _i, _i64, _vp, _vp, _vp, _vp, _vp, _i, _vp, _f, _vp]),
     "isp_scaled_gemm": (_i, [_vp, _vp, _i, _i64, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _vp, _i, _f, _vp, _f, _vp]),
     "isp_gated_up": (_i, [_vp, _vp, _vp, _i, _i64, _i, _i, _vp, _vp, _f, _vp, _i, _vp]),

@@ -356,6 +356,12 @@ int out_kind_of(int dtype) {
 }  // namespace gemm
 }  // namespace isp
 
+// Per-utterance |x| maxima of isp_conv1d_dynamic_noalloc, kept in the library instead
+// of a caller buffer.  One region per process and device: calls that overlap in time
+// (two streams, two host threads) race on it.
+constexpr int64_t kConvNoAllocMaxBatch = 8192;
+static __device__ __align__(256) float g_conv_amax_scratch[kConvNoAllocMaxBatch];
+
 extern "C" {
 
 int isp_version(void) { return 100; }
@@ -876,6 +882,38 @@ int isp_nvfp4_gated_up(const void* A, const void* A_sf, const void* W13, const v
         ta, tb, tb, ta, p, stream);
   return launch<kFp4BN, kFp4Stages, kFp4SwigluEpiWarps, AB_FP4, EPI_SWIGLU_PAIRED, OUT_NVFP4>(ta, tb, tb, ta, p,
                                                                                           stream);
+}
+
+// ---- dynamic-scale convolution without caller scratch (array above extern "C") ----
+int isp_conv1d_dynamic_noalloc(const void* x, int x_dtype, int64_t B, int C, int64_t T, void* xq, int C_pad,
+                               const void* w_packed, int CO, int KW, int stride, int dilation, int padding,
+                               int output_padding, int transposed, int64_t T_out, const float* w_scale,
+                               const float* bias, void* y, int out_dtype, isp_stream_t stream) {
+  if (B > kConvNoAllocMaxBatch) return ISP_ERR_SHAPE;   // more utterances than the scratch holds
+  if (x == nullptr || xq == nullptr || w_packed == nullptr || w_scale == nullptr || y == nullptr) return ISP_ERR_ARG;
+  if (B < 0) return ISP_ERR_SHAPE;
+  if (int st = isp::check_device()) return st;
+  // Scratch address of the current device, resolved on that device's first call.
+  static float* amax_of[64] = {nullptr};
+  static std::mutex setup;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ISP_ERR_ARCH;
+  float* amax = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(setup);
+    if (amax_of[dev] == nullptr) {
+      void* addr = nullptr;
+      if (cudaGetSymbolAddress(&addr, g_conv_amax_scratch) != cudaSuccess || addr == nullptr) return ISP_ERR_LAUNCH;
+      amax_of[dev] = static_cast<float*>(addr);
+    }
+    amax = amax_of[dev];
+  }
+  // isp_conv1d_quant clears amax[0 .. B) before its maximum pass
+  const int row_multiple = transposed ? 1 : stride;
+  if (int st = isp_conv1d_quant(x, x_dtype, B, C, T, row_multiple, nullptr, 0.f, amax, ISP_E4M3, xq, C_pad, stream))
+    return st;
+  return isp_conv1d(xq, ISP_E4M3, B, C_pad, T, w_packed, CO, KW, stride, dilation, padding, output_padding,
+                    transposed, T_out, 0.f, amax, w_scale, bias, y, out_dtype, stream);
 }
 
 }  // extern "C"
