@@ -646,6 +646,9 @@ int isp_fir_snake(const float* x, int64_t rows, int C, int64_t T, const float* u
     p.up2[k] = 2.f * up[k];
     p.down[k] = down[k];
   }
+  for (int m = 0; m < 6; ++m) p.upp[m] = make_float2(p.up2[11 - 2 * m], p.up2[10 - 2 * m]);
+  for (int k = 0; k < 5; ++k) p.dnp[k] = make_float2(p.down[2 * k + 1], p.down[2 * k + 2]);
+  p.rscale = 1.f / scale;   // RN(1/s) (IEEE single-precision division on the host)
   auto kern = out_dtype == ISP_F32 ? (bulk ? isp::fir_snake_kernel<false, true> : isp::fir_snake_kernel<false, false>)
                                    : (bulk ? isp::fir_snake_kernel<true, true> : isp::fir_snake_kernel<true, false>);
   static bool configured[4][64] = {{false}};

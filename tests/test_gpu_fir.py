@@ -29,7 +29,8 @@ def _params(c, seed):
     return alpha, torch.from_numpy(ofir.snake_inverse_beta(alpha.numpy()))
 
 
-@pytest.mark.parametrize("b,c,t", [(1, 1, 1), (1, 3, 2), (2, 4, 5), (1, 2, 2047), (1, 2, 2048), (1, 2, 2049),
+@pytest.mark.parametrize("b,c,t", [(1, 1, 1), (1, 3, 2), (2, 4, 5), (1, 2, 1023), (1, 2, 1025), (2, 3, 1028),
+                                   (1, 2, 2047), (1, 2, 2048), (1, 2, 2049),
                                    (2, 8, 4095), (1, 4, 6145), (3, 5, 301),
                                    # T % 4 == 0: streamed by bulk copies, incl. tiles that end past T
                                    (1, 1, 4), (2, 3, 8), (1, 2, 12), (1, 3, 2052), (2, 2, 4100), (1, 3, 6144),
