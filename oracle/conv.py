@@ -91,15 +91,20 @@ def fp8_conv1d(x, w, bias, in_scale, w_scale, *, dilation=1, padding=0, fmt="e4m
 
 
 def fp8_conv_transpose1d(x, w_t, bias, in_scale, w_scale, *, stride, padding=0, output_padding=0, dilation=1,
-                         fmt="e4m3"):
+                         fmt="e4m3", smooth=None):
     """ConvTranspose1d (weight [CI, CO, KW], w_scale per output channel) through
     the zero-insertion rewrite: transposed, flipped weight; input zero-inserted by
-    the stride and padded (pad, pad + output_padding), pad = dil (KW-1) - padding."""
-    w = np.ascontiguousarray(np.flip(np.transpose(np.asarray(w_t, np.float32), (1, 0, 2)), -1))
+    the stride and padded (pad, pad + output_padding), pad = dil (KW-1) - padding.
+    INT8 SmoothQuant: the weight is multiplied by smooth along CI (its axis 0,
+    ``build/unified_acoustic_export.py:108-111``) and the input divided by it."""
+    w_t = np.asarray(w_t, np.float32)
+    if smooth is not None:
+        w_t = (w_t * np.asarray(smooth, np.float32)[:, None, None]).astype(np.float32)
+    w = np.ascontiguousarray(np.flip(np.transpose(w_t, (1, 0, 2)), -1))
     kw = w.shape[-1]
     pad = dilation * (kw - 1) - padding
     xi = zero_insert(np.asarray(x, np.float32), stride)
-    xq = quantize_input(xi, in_scale, fmt)
+    xq = quantize_input(xi, in_scale, fmt, smooth)
     wq = quantize_weight(w, w_scale, fmt)
     t_out = xq.shape[-1] + 2 * pad + output_padding - dilation * (kw - 1)
     acc = conv1d_codes(xq, wq, fmt, dilation, pad, t_out).astype(np.float32)

@@ -198,3 +198,28 @@ def test_fp8_matrix_conv_module(C):
     assert rel_l2(y.detach().cpu().numpy(), ref) < 1e-5
     # two calls in a row reuse the cached folded weight
     assert torch.equal(m(x), y)
+
+
+def test_export_int8_smoothquant_deconv_vs_oracle(C):
+    """INT8 SmoothQuant ConvTranspose1d role (smoothing on the CI axis of the
+    [CI, CO, KW] weight, input divided before the zero insertion): exact integer
+    products, so the folded phases match the zero-insertion oracle to FP32 rounding."""
+    ci, co, kw, s, pad = 144, 48, 8, 4, 2
+    g = np.random.default_rng(13)
+    deconv = torch.nn.ConvTranspose1d(ci, co, kw, stride=s, padding=pad)
+    with torch.no_grad():
+        deconv.weight.copy_(torch.from_numpy((g.standard_normal((ci, co, kw)) * 0.05).astype(np.float32)))
+    x = g.standard_normal((2, ci, 37)).astype(np.float32)
+    x[:, :4] *= 15
+    smooth = (np.sqrt(np.abs(x).max(axis=(0, 2))) + 0.5).astype(np.float32)
+    in_scale = float(np.abs(x / smooth[None, :, None]).max() / 127)
+    wsm = deconv.weight.detach().numpy() * smooth[:, None, None]
+    w_s = (np.abs(wsm).max(axis=(0, 2)) / 127).astype(np.float32)
+    q = C.QuantConv1d(deconv.cuda(), {"precision": "int8", "input_scale": in_scale, "weight_scale": w_s.tolist(),
+                                      "weight_axis": 1, "smooth_scale": smooth.tolist(),
+                                      "conv_transpose_rewrite": "zero_insert_conv"})
+    ref = oconv.fp8_conv_transpose1d(x, deconv.weight.detach().cpu().numpy(), deconv.bias.detach().cpu().numpy(),
+                                     in_scale, w_s, stride=s, padding=pad, fmt="int8", smooth=smooth)
+    y = q(torch.from_numpy(x).cuda()).cpu().numpy()
+    assert y.shape == ref.shape
+    assert rel_l2(y, ref) < 1e-6
