@@ -326,7 +326,8 @@ int isp_nvfp4_gated_up(const void *A, const void *A_sf, const void *W13, const v
  * array inside the library instead of a caller buffer.  xq is still the caller's
  * [B, T_rows, C_pad] code buffer (sized as for isp_conv1d_quant); every other
  * argument as isp_conv1d.
- *   - B <= 8192 (ISP_ERR_SHAPE beyond); the call allocates nothing.
+ *   - B <= 8192 (ISP_ERR_SHAPE beyond); the call allocates nothing.  The array is
+ *     8192 floats (32 KB), held by every GPU that loads the library until exit.
  *   - The first call on each device resolves the array's address on that device
  *     (device must be current); make that first call before any stream capture.
  *   - The maxima are cleared at the start of each call.  One array per process and
