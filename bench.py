@@ -309,8 +309,9 @@ def fir_component(torch, device, hbm_peak):
 def run_case(args, torch, device, hbm_peak, bf16_peak):
     """Single-kernel cases (profiling targets), each timed launch after a 256 MB L2
     flush: gemm = the dominant cfg-2 projection, norm_quant = cfg-2 norm-quant,
-    fir = one cfg-5 micro-batch (B16 with --small), nvfp4_* = config 3, int8_decode =
-    config 4's decode projections, conv / deconv / conv_quant = BigVGAN learned convs."""
+    fir / fir_c256 = one cfg-5 micro-batch of either shape (B16 with --small), nvfp4_* =
+    config 3, int8_decode / int8_prefill = config 4's projections at M = 64 / 16384,
+    conv / deconv / conv_quant = BigVGAN learned convs."""
     from inspark_proper_format_b200 import _lib
     lib = _lib.load()
     stream = torch.cuda.current_stream(device).cuda_stream
@@ -376,6 +377,34 @@ def run_case(args, torch, device, hbm_peak, bf16_peak):
         fargs = ()
         flops = sum(2 * m * n * k for _, n, k in shapes)
         name = "int8 decode M=64: qkv 1280->3840, out 1280->1280, up 1280->5120, down 5120->1280 (4 launches)"
+    elif args.case == "int8_prefill":
+        # config 4 prefill: M = 64 x 256 tokens through the AR model's four projections,
+        # INT8 SmoothQuant codes, BF16 out, launched back to back
+        m = 64 * 256
+        shapes = [("qkv", 3840, 1280), ("out", 1280, 1280), ("mlp_up", 5120, 1280), ("mlp_down", 1280, 5120)]
+        calls = []
+        nbytes = 0
+        keep = []
+        for _, n, k in shapes:
+            a = torch.randint(-127, 128, (m, k), device=device, generator=g, dtype=torch.int8)
+            w = torch.randint(-127, 128, (n, k), device=device, generator=g, dtype=torch.int8)
+            ws = torch.rand(n, device=device, generator=g) * 1e-3
+            bias = torch.rand(n, device=device, generator=g)
+            out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+            keep += [a, w, ws, bias, out]
+            calls.append((a.data_ptr(), w.data_ptr(), _lib.I8, m, n, k, 0.01, None, ws.data_ptr(), bias.data_ptr(),
+                          None, _lib.F32, out.data_ptr(), _lib.BF16, 1.0, None, 0.0, stream))
+            nbytes += m * k + n * k + m * n * 2 + 8 * n
+
+        def fn(*_):
+            for c in calls:
+                st = lib.isp_scaled_gemm(*c)
+                if st:
+                    return st
+            return 0
+        fargs = ()
+        flops = sum(2 * m * n * k for _, n, k in shapes)
+        name = "int8 prefill M=16384: qkv 1280->3840, out 1280->1280, up 1280->5120, down 5120->1280 (4 launches)"
     elif args.case in ("nvfp4_gated_up", "nvfp4_down"):
         # config 3: gated-up M=51200, K=512, N=2x2048 (NVFP4 h out), down 2048 -> 512 (BF16 out)
         m = 51200
@@ -449,7 +478,8 @@ def run_case(args, torch, device, hbm_peak, bf16_peak):
         import ctypes
 
         from inspark_proper_format_b200.alias_free import host_taps, kaiser_sinc_filter, snake_inverse_beta
-        b, c, t = (16 if args.small else 64), 512, 16384
+        b = 16 if args.small else 64
+        c, t = (256, 65536) if args.case == "fir_c256" else (512, 16384)   # config 5's two shapes
         x = torch.randn(b, c, t, device=device, generator=g) * 0.5
         y = torch.empty_like(x)
         taps = host_taps(kaiser_sinc_filter())
@@ -482,7 +512,8 @@ def run_case(args, torch, device, hbm_peak, bf16_peak):
     if flops:
         line["TFLOP/s"] = round(flops / sec / 1e12, 1)
         fp4 = args.case.startswith("nvfp4")
-        line["frac_fp4" if fp4 else "frac_fp8"] = round(flops / sec / 1e12 / ((4 if fp4 else 2) * bf16_peak), 3)
+        key = "frac_fp4" if fp4 else ("frac_int8" if args.case.startswith("int8") else "frac_fp8")
+        line[key] = round(flops / sec / 1e12 / ((4 if fp4 else 2) * bf16_peak), 3)   # INT8 dense rate = FP8's
     print(json.dumps(line), flush=True)
 
 
@@ -565,7 +596,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-components", action="store_true")
     ap.add_argument("--case", choices=("stack", "gemm", "norm_quant", "fir", "nvfp4_gated_up", "nvfp4_down",
-                                       "conv", "deconv", "conv_quant",
+                                       "conv", "deconv", "conv_quant", "int8_prefill", "fir_c256",
                                        "int8_decode"),
                     default="stack",
                     help="stack = the headline step; the others time one kernel (profiling targets)")
