@@ -28,6 +28,27 @@ inline int launch_status() {
   return e == cudaSuccess ? ISP_OK : ISP_ERR_LAUNCH;
 }
 
+// Launch with programmatic stream serialization: the kernel may be scheduled while
+// its predecessor in the stream finishes, and must call pdl_wait() before touching
+// global memory.  Returns an isp_status.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  (void)cudaGetLastError();   // the status is returned here, not left for a later launch_status()
+  return e == cudaSuccess ? ISP_OK : ISP_ERR_LAUNCH;
+}
+
 // Device error word (one per device; the library is a single translation unit).
 __device__ int g_device_error = 0;
 
@@ -97,6 +118,14 @@ ISP_D int8_t int8_rne_sat(float v) {
 }
 
 ISP_D float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while its predecessor in the stream is still running;
+// pdl_wait() blocks until that predecessor has completed and its writes are visible
+// (a no-op for an ordinary launch), so no global memory may be read or written
+// before it.  pdl_trigger() lets the next such kernel start its own prologue.
+ISP_D void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+ISP_D void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // RN to BF16 of (lo, hi) in one conversion: lo in bits 0-15, hi in bits 16-31.
 ISP_D uint32_t pack_bf16_rn(float lo, float hi) {

@@ -820,6 +820,10 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const S sched(p);
+  // The prologue above touches no global memory; from here on the kernel reads its
+  // predecessor's outputs, so wait for it, then let the next kernel start early.
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer

@@ -182,8 +182,7 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, co
   }
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, Roles<kEpiWarps>::kThreads, kSmem, stream>>>(a, b, b2, o, p);
-  return launch_status();
+  return launch_pdl(kern, dim3(grid), dim3(Roles<kEpiWarps>::kThreads), kSmem, stream, a, b, b2, o, p);
 }
 
 template <int kAB, int kOut>

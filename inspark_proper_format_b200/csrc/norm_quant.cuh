@@ -77,6 +77,8 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
   const int lane = threadIdx.x % kLanes;   // lane within the row
   const int64_t row = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * (32 / kLanes) +
                       (threadIdx.x & 31) / kLanes;
+  pdl_wait();       // predecessor's output (this kernel's input) complete and visible
+  pdl_trigger();
   const bool active = row < p.M;
   if (__all_sync(0xffffffffu, !active)) return;
   const int K = p.K;
@@ -258,22 +260,18 @@ int launch_norm_quant_groups(const NormQuantParams& p, cudaStream_t stream) {
   const dim3 block(256);
   if (p.K <= 512) {   // half-warp rows: 16 rows per block, up to 4 groups per lane
     const dim3 grid(static_cast<unsigned>((p.M + 15) / 16));
-    if (p.K <= 256) norm_quant_kernel<kBF16, kNorm, kFmt, 2, 16><<<grid, block, 0, stream>>>(p);
-    else norm_quant_kernel<kBF16, kNorm, kFmt, 4, 16><<<grid, block, 0, stream>>>(p);
-    return launch_status();
+    if (p.K <= 256) return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 2, 16>, grid, block, 0, stream, p);
+    return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 4, 16>, grid, block, 0, stream, p);
   }
   const int per_lane = (p.K / 8 + 31) / 32;
   const dim3 grid(static_cast<unsigned>((p.M + 7) / 8));
-  if (per_lane <= 4) norm_quant_kernel<kBF16, kNorm, kFmt, 4, 32><<<grid, block, 0, stream>>>(p);
-  else if (per_lane <= 8) norm_quant_kernel<kBF16, kNorm, kFmt, 8, 32><<<grid, block, 0, stream>>>(p);
-  else if (per_lane <= 16) norm_quant_kernel<kBF16, kNorm, kFmt, 16, 32><<<grid, block, 0, stream>>>(p);
-  else if constexpr (kNorm == ISP_NORM_NONE) {
-    if (per_lane <= 32) norm_quant_kernel<kBF16, kNorm, kFmt, 32, 32><<<grid, block, 0, stream>>>(p);
-    else return ISP_ERR_SHAPE;
-  } else {
-    return ISP_ERR_SHAPE;
+  if (per_lane <= 4) return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 4, 32>, grid, block, 0, stream, p);
+  if (per_lane <= 8) return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 8, 32>, grid, block, 0, stream, p);
+  if (per_lane <= 16) return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 16, 32>, grid, block, 0, stream, p);
+  if constexpr (kNorm == ISP_NORM_NONE) {
+    if (per_lane <= 32) return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 32, 32>, grid, block, 0, stream, p);
   }
-  return launch_status();
+  return ISP_ERR_SHAPE;
 }
 
 template <bool kBF16, int kNorm>
