@@ -126,6 +126,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const bool run = aligned;
+  pdl_wait();      // predecessor complete before any operand or output access
+  pdl_trigger();
 
   if (warp == 0 && run) {
     // ------------------------------------------------------------ producer

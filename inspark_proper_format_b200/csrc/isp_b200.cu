@@ -252,13 +252,15 @@ int launch_decode(const CUtensorMap& a, const CUtensorMap& b, const Params& p, i
   cfg.blockDim = dim3(kDecThreads, 1, 1);
   cfg.dynamicSmemBytes = DecSmem::kBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see pdl_wait()
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, kern, a, b, p, splits) != cudaSuccess) {
     cudaGetLastError();
     return ISP_ERR_LAUNCH;
