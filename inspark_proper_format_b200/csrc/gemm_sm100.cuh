@@ -108,6 +108,8 @@ struct Params {
   int conv_tma_store;     // 1: output blocks of 32 rows x 32 columns leave through the
                           // [B, CO, T_out] tensor map (boxes of 32/P channels x 32P times)
   int conv_tab[kConvTab];
+  // Streaming scale epilogue: run the last partial wave as half-N tiles (two per tile)
+  int tail_split;
 };
 
 // Shared-memory layout.  Streaming (kBStatK == 0): stage s = [A | B | A scales | B scales].
@@ -721,8 +723,10 @@ ISP_D uint2 swiglu_nvfp4_block(const uint32_t (&a)[16], const uint32_t (&b)[16],
 template <bool kStat>
 struct Schedule {
   int begin, end, step;
+  int full;   // streaming with tail_split: units from here on are half-N tiles, two per tile
   ISP_D Schedule(const Params& p) {
     const int total = p.m_tiles * p.n_tiles;
+    full = total;
     if constexpr (kStat) {
       begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * total / gridDim.x);
       end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x);
@@ -731,9 +735,24 @@ struct Schedule {
       begin = blockIdx.x;
       end = total;
       step = gridDim.x;
+      // The last partial wave (rem tiles) would keep rem CTAs busy while the rest idle;
+      // as 2 rem half-N tiles it spreads over twice as many CTAs.
+      const int rem = total % static_cast<int>(gridDim.x);
+      if (p.tail_split && rem > 0 && 2 * rem <= static_cast<int>(gridDim.x)) {
+        full = total - rem;
+        end = total + rem;
+      }
     }
   }
-  ISP_D static void coords(const Params& p, int t, int& mt, int& nt) {
+  // Unit t -> tile (mt, nt); hn = -1 for a whole tile, else the N half (0 / 1) of a split tile.
+  ISP_D void coords(const Params& p, int t, int& mt, int& nt, int& hn) const {
+    hn = -1;
+    if constexpr (!kStat) {
+      if (t >= full) {
+        hn = (t - full) & 1;
+        t = full + ((t - full) >> 1);
+      }
+    }
     if constexpr (kStat) {
       nt = t / p.m_tiles;
       mt = t - nt * p.m_tiles;
@@ -839,8 +858,8 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
       int cur_nt = -1;
       uint32_t nloads = 0;                       // resident-B loads issued
       for (int t = sched.begin; t < sched.end && ok; t += sched.step) {
-        int mt, nt;
-        S::coords(p, t, mt, nt);
+        int mt, nt, hn;
+        sched.coords(p, t, mt, nt, hn);   // a half-N tile loads the whole tile's A and B
         const int m0 = mt * kBM;
         if constexpr (kStat) {
           if (nt != cur_nt) {
@@ -918,6 +937,7 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     // The whole warp runs the loop (waits converged); lane 0 issues tcgen05 ops.
     {
       const uint32_t idesc = instr_desc<kAB, kBN>();
+      const uint32_t idesc_half = instr_desc<kAB, kBN / 2>();   // half-N tiles of the split tail
       const uint32_t sfb_res_t = tmem_base + static_cast<uint32_t>(2 * kBN);   // B-stationary NVFP4
       int stage = 0;
       uint32_t phase = 0;
@@ -928,8 +948,8 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
       int cur_nt = -1;
       uint32_t bphase = 0;
       for (int t = sched.begin; t < sched.end && ok; t += sched.step) {
-        int mt, nt;
-        S::coords(p, t, mt, nt);
+        int mt, nt, hn;
+        sched.coords(p, t, mt, nt, hn);
         (void)mt;
         if constexpr (kStat) {
           if (nt != cur_nt) {
@@ -976,9 +996,12 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
                         sfa_t + 4 * kk, sfb_t, (kb | kk) != 0);
               }
             } else {
+              // half-N tile: N = kBN / 2 on B rows [hn kBN / 2, (hn + 1) kBN / 2) of the stage
+              const uint32_t bh = hn > 0 ? b_addr + static_cast<uint32_t>((kBN / 2) * kBK) : b_addr;
+              const uint32_t id = hn >= 0 ? idesc_half : idesc;
 #pragma unroll
               for (int kk = 0; kk < kBK / 32; ++kk) {
-                mma_issue<kInt8>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
+                mma_issue<kInt8>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(bh + kk * 32), id,
                                  (kb | kk) != 0);
               }
             }
@@ -1016,8 +1039,8 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = sched.begin; t < sched.end; t += sched.step) {
-        int mt, nt;
-        S::coords(p, t, mt, nt);
+        int mt, nt, hn;
+        sched.coords(p, t, mt, nt, hn);   // (never split: the scale epilogue only)
         const int m = mt * kBM + quarter * 32 + lane;
         const int n = nt * (kBN / 2) + 16 * blk;    // first output column of this block
         if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
@@ -1056,27 +1079,36 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
       constexpr int kWordsPerGroup = 32 / kGroupsPerChunk;
       TileParams<kEpi, kBN, R::kEpiThreads> tp;
       if (sched.begin < sched.end) {
-        int mt, nt;
-        S::coords(p, sched.begin, mt, nt);
-        tp.fetch(p, nt * kOutCols, et);
+        int mt, nt, hn;
+        sched.coords(p, sched.begin, mt, nt, hn);
+        tp.fetch(p, nt * kOutCols + (hn > 0 ? kOutCols / 2 : 0), et);
       }
       for (int t = sched.begin; t < sched.end; t += sched.step) {
-        int mt, nt;
-        S::coords(p, t, mt, nt);
+        int mt, nt, hn;
+        sched.coords(p, t, mt, nt, hn);
         const int m0 = mt * kBM;
-        const int n0 = nt * kOutCols;
+        const int n0 = nt * kOutCols + (hn > 0 ? kOutCols / 2 : 0);   // half-N tile: its columns
         // Per-column parameters of this tile -> shared memory (zero past column N),
         // then start fetching the next tile's.
         epilogue_sync<R::kEpiThreads>();
         tp.store(params, et);
         epilogue_sync<R::kEpiThreads>();
         if (t + sched.step < sched.end) {
-          int mt2, nt2;
-          S::coords(p, t + sched.step, mt2, nt2);
-          tp.fetch(p, nt2 * kOutCols, et);
+          int mt2, nt2, hn2;
+          sched.coords(p, t + sched.step, mt2, nt2, hn2);
+          tp.fetch(p, nt2 * kOutCols + (hn2 > 0 ? kOutCols / 2 : 0), et);
         }
         if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
         tc_fence_after();
+        if (hn >= 0 && half == 1) {
+          // a half-N tile fills accumulator columns [0, kBN / 2) only: nothing for the
+          // warps of the upper columns but handing the accumulator back
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+          if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+          continue;
+        }
         const int m = m0 + row_in_tile;
         // EPI_CONV: the row is phase row cq of utterance cu (output times cq * P + r)
         const int cu = kEpi == EPI_CONV ? mt / p.conv_tpb : 0;

@@ -157,6 +157,15 @@ bool streaming_forced() {
   return forced;
 }
 
+// ISP_GEMM_NO_TAIL_SPLIT=1 keeps the last partial wave of streaming GEMMs as whole tiles.
+bool tail_split_disabled() {
+  static const bool off = [] {
+    const char* v = getenv("ISP_GEMM_NO_TAIL_SPLIT");
+    return v != nullptr && v[0] == '1';
+  }();
+  return off;
+}
+
 // ISP_CONV_DIRECT_STORE=1 keeps the convolution epilogue on per-element stores.
 bool conv_direct_forced() {
   static const bool forced = [] {
@@ -737,6 +746,9 @@ int isp_scaled_gemm(const void* A, const void* W, int ab_dtype, int64_t M, int N
   p.out2 = out2;
   p.out2_inv = out2_inv_scale;
   const bool stat = K <= kStatK && !streaming_forced();
+  // streaming: the last partial wave runs as half-N tiles (needs the two-warps-per-quarter
+  // epilogue, whose upper warps simply hand a half tile's accumulator back)
+  p.tail_split = !stat && kScaleEpiWarps == 8 && !tail_split_disabled();
   return ab_dtype == ISP_I8 ? dispatch_scale_out<AB_I8>(out_kind, stat, ta, tb, to, p, stream)
                             : dispatch_scale_out<AB_E4M3>(out_kind, stat, ta, tb, to, p, stream);
 }

@@ -259,3 +259,45 @@ def test_fp8_decode_row_scales_residual(G, m, n, k):
                       residual=res.cuda(), out_dtype=torch.float16)
     ref = og.fp8_gemm(a, w, rows, sw, bias, residual=res.float().numpy(), out="f32")
     assert rel_l2(y.float().cpu().numpy(), ref) < 1e-3      # F16 output rounding
+
+
+# Streaming launches (K > 512) with more tiles than SMs run their last partial wave as
+# half-N tiles: 9600 rows x N=512 is 150 tiles (2 split into 4 halves), the cfg-2
+# ff_out shape 760 tiles (20 split into 40).
+@pytest.mark.parametrize("m,n,k", [(9600, 512, 1536), (48640, 512, 1536), (9600, 1024, 1040)])
+def test_fp8_streaming_tail_split(G, m, n, k):
+    a, w, sa, sw, bias = fp8_operands(m, n, k, 31)
+    y = G.scaled_gemm(dev_codes(a), dev_codes(w), a_scale=float(sa), w_scale=torch.from_numpy(sw).cuda(),
+                      bias=torch.from_numpy(bias).cuda(), out_dtype=torch.float32)
+    ref = og.fp8_gemm(a, w, sa, sw, bias, out="f32")
+    got = y.cpu().numpy()
+    assert rel_l2(got, ref) < 1e-6
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5 * np.abs(ref).max())
+
+
+def test_int8_streaming_tail_split_bit_exact(G):
+    m, n, k = 9600, 1024, 1280                         # 300 tiles: 4 split into 8 halves
+    g = np.random.default_rng(41)
+    qa = g.integers(-128, 128, (m, k), dtype=np.int64).astype(np.int8)
+    qw = g.integers(-127, 128, (n, k), dtype=np.int64).astype(np.int8)
+    sa = np.float32(1 / 127)
+    sw = (g.random(n).astype(np.float32) * 1e-3 + 1e-4).astype(np.float32)
+    bias = (g.standard_normal(n) * 0.1).astype(np.float32)
+    r = g.standard_normal((m, n)).astype(np.float32)
+    y = G.i8_residual(torch.from_numpy(qa).cuda(), torch.from_numpy(qw).cuda(), float(sa), torch.from_numpy(sw).cuda(),
+                      torch.from_numpy(bias).cuda(), torch.from_numpy(r).cuda())
+    ref = og.int8_gemm(qa, qw, sa, sw, bias, r)
+    np.testing.assert_array_equal(y.cpu().numpy(), ref)
+
+
+def test_residual_dual_output_tail_split(G):
+    m, n, k = 9600, 512, 1024                          # 150 tiles: residual + dual E4M3 on half tiles
+    a, w, sa, sw, bias = fp8_operands(m, n, k, 7)
+    alpha = np.float32(sa * sw.mean())
+    r = np.random.default_rng(3).standard_normal((m, n)).astype(np.float32)
+    inv = np.float32(30.0)
+    y, q = G.fused_projection_residual(dev_codes(a), dev_codes(w), torch.from_numpy(bias).cuda(),
+                                       torch.from_numpy(r).cuda(), float(alpha), float(inv))
+    zref, qref = og.residual_dual(a, w, alpha, bias, r, inv)
+    assert rel_l2(y.cpu().numpy(), zref) < 1e-6
+    assert np.mean(q.view(torch.uint8).cpu().numpy() != qref) < 1e-3
