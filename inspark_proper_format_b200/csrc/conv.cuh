@@ -115,6 +115,60 @@ __global__ void __launch_bounds__(256) conv_quant_kernel(ConvQuantParams p) {
   const int64_t t = t0 + r;
   const int64_t base = (b * p.C + c0) * p.T + t;
   const bool interior = t0 + kCqRows <= p.T && c0 + 128 <= p.C;   // block-uniform
+  // FP32 interior tiles with 16-byte aligned rows: a thread takes 4 consecutive rows x 4
+  // channels and reads each channel's 4 samples as one float4 (half-warps cover 256
+  // contiguous bytes of one channel); block-uniform.
+  if constexpr (!kBf16) {
+    if (interior && (p.T & 3) == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int k = threadIdx.x + 256 * i;
+        const int rg = k % (kCqRows / 4);          // group of 4 rows
+        const int quad = k / (kCqRows / 4);        // group of 4 channels
+        const float* src = static_cast<const float*>(p.x) + (b * p.C + c0 + quad * 4) * p.T + t0 + 4 * rg;
+        float4 v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = __ldg(reinterpret_cast<const float4*>(src + j * p.T));
+        float col[4][4];   // [row][channel]
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          col[0][j] = v[j].x;
+          col[1][j] = v[j].y;
+          col[2][j] = v[j].z;
+          col[3][j] = v[j].w;
+        }
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+          uint32_t word;
+          if constexpr (kInt8) {
+            word = 0u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float u = col[rr][j];
+              if (p.smooth != nullptr) u = __fdiv_rn(u, __ldg(p.smooth + c0 + quad * 4 + j));
+              word |= static_cast<uint32_t>(static_cast<uint8_t>(int8_rne_sat(div_rn_recip(u, scale, rscale))))
+                      << (8 * j);
+            }
+          } else {
+            word = static_cast<uint32_t>(e4m3x2(div_rn_recip(col[rr][0], scale, rscale),
+                                                div_rn_recip(col[rr][1], scale, rscale))) |
+                   static_cast<uint32_t>(e4m3x2(div_rn_recip(col[rr][2], scale, rscale),
+                                                div_rn_recip(col[rr][3], scale, rscale)))
+                       << 16;
+          }
+          tile[(4 * rg + rr) * kCqPitch + quad] = word;
+        }
+      }
+      __syncthreads();
+#pragma unroll 2
+      for (int k = threadIdx.x; k < kCqRows * 32; k += 256) {
+        const int rr = k / 32;
+        const int w = k % 32;
+        reinterpret_cast<uint32_t*>(p.xq + (b * p.t_rows + t0 + rr) * p.c_pad + c0)[w] = tile[rr * kCqPitch + w];
+      }
+      return;
+    }
+  }
 #pragma unroll 2
   for (int i = 0; i < 8; ++i) {
     const int quad = quad0 + 4 * i;

@@ -148,13 +148,14 @@ def test_export_conv_roles_match_reference_fixture(C):
     assert rel_l2(yd, d["yd"]) < 1e-5
 
 
-def test_export_int8_smoothquant_conv_vs_oracle(C):
+@pytest.mark.parametrize("t", [150, 160])            # scalar and float4 input loads
+def test_export_int8_smoothquant_conv_vs_oracle(C, t):
     ci, co, kw, pad, dil = 136, 64, 5, 4, 2
     g = np.random.default_rng(11)
     conv = torch.nn.Conv1d(ci, co, kw, padding=pad, dilation=dil)
     with torch.no_grad():
         conv.weight.copy_(torch.from_numpy((g.standard_normal((co, ci, kw)) * 0.05).astype(np.float32)))
-    x = g.standard_normal((2, ci, 150)).astype(np.float32)
+    x = g.standard_normal((2, ci, t)).astype(np.float32)
     x[:, :3] *= 12
     smooth = np.sqrt(np.abs(x).max(axis=(0, 2)) / 4).astype(np.float32) + np.float32(0.5)
     in_scale = float(np.abs(x / smooth[None, :, None]).max() / 127)
