@@ -54,8 +54,27 @@ def synthetic_export(seed=0):
                                  "weight_scale": [0.01] * 64, "weight_axis": 0, "weight_input_axis": 1}
     state["conv_pre.weight.weight_scale"] = torch.full((64,), 0.01)
     state["conv_pre.weight.input_scale"] = torch.tensor(0.1)
+    state["conv_pre.bias"] = torch.randn(64, generator=g) * 0.1
+    # INT8 SmoothQuant ConvTranspose1d role ([CI, CO, KW]: scales on axis 1, smoothing on 0)
+    w = torch.randn(32, 24, 8, generator=g) * 0.05
+    smooth = torch.rand(32, generator=g) + 0.5
+    w = w * smooth[:, None, None]
+    scale = (w.abs().amax(dim=(0, 2)) / 127).clamp_min(1e-12)
+    key = "ups.0.0.weight"
+    state[key] = (w / scale[None, :, None]).round().clamp(-128, 127).to(torch.int8)
+    state[key + ".weight_scale"] = scale
+    state[key + ".input_scale"] = torch.tensor(0.02)
+    state[key + ".smooth_scale"] = smooth
+    state["ups.0.0.bias"] = torch.randn(24, generator=g) * 0.1
+    roles["vocoder.stages.0.ups.0"] = {"precision": "int8", "state_key": key, "input_scale": 0.02,
+                                       "weight_scale": scale.tolist(), "smooth_scale": smooth.tolist(),
+                                       "weight_axis": 1, "weight_input_axis": 0}
     meta = {"component": "cfm", "scheme": "mixed", "roles": roles}
     return state, meta
+
+
+CONV_GEOMETRY = {"vocoder.conv_pre": {"stride": 1, "padding": 3, "dilation": 1},
+                 "vocoder.stages.0.ups.0": {"stride": 4, "padding": 2, "dilation": 1, "transposed": True}}
 
 
 def test_artifact_validation_rules():
@@ -97,7 +116,7 @@ def test_exported_roles_run_on_the_kernels():
     from inspark_proper_format_b200.manifest import load_component_bytes
     state, meta = synthetic_export(1)
     roles, skipped = load_component_bytes(save(state), meta)
-    assert set(skipped) == {"vocoder.conv_pre"}
+    assert set(skipped) == {"vocoder.conv_pre", "vocoder.stages.0.ups.0"}     # no geometry given
     x = torch.randn(96, 256, generator=torch.Generator().manual_seed(2))
     xf = x.numpy()
     # fp8: static E4M3 Q then acc * input_scale * weight_scale + bias
@@ -126,3 +145,37 @@ def test_exported_roles_run_on_the_kernels():
     y = roles["cfm.proj"](x.cuda(), out_dtype=torch.float32).cpu()
     ref = torch.nn.functional.linear(x.bfloat16(), state["proj.weight"]).float()
     assert torch.allclose(y, ref, rtol=1e-2, atol=1e-3)
+
+
+@pytest.mark.gpu
+def test_exported_conv_roles_run_on_the_conv_kernels():
+    """fp8 Conv1d and INT8 SmoothQuant ConvTranspose1d roles with the caller's geometry:
+    static input Q (INT8: divided by the smoothing factors), exact code sums, then
+    ``acc * input_scale * weight_scale[co] + bias`` (``ExportWeightOp`` conv roles)."""
+    from safetensors.torch import save
+    from inspark_proper_format_b200.manifest import load_component_bytes
+    from oracle import conv as oconv
+    state, meta = synthetic_export(3)
+    roles, skipped = load_component_bytes(save(state), meta, conv_geometry=CONV_GEOMETRY)
+    assert not skipped
+    g = torch.Generator().manual_seed(4)
+    for role, key, ci, fmt in (("vocoder.conv_pre", "conv_pre.weight", 32, "e4m3"),
+                               ("vocoder.stages.0.ups.0", "ups.0.0.weight", 32, "int8")):
+        geo = CONV_GEOMETRY[role]
+        tr = geo.get("transposed", False)
+        x = torch.randn(2, ci, 48, generator=g) * 2
+        y = roles[role](x.cuda(), out_dtype=torch.float32).cpu().numpy()
+        s_in = np.float32(state[key + ".input_scale"])
+        smooth = state.get(key + ".smooth_scale")
+        xq = oconv.quantize_input(x.numpy(), s_in, fmt, None if smooth is None else smooth.numpy())
+        codes = state[key]
+        codes = codes.view(torch.uint8) if fmt == "e4m3" else codes
+        wq = codes.permute(1, 0, 2).numpy() if tr else codes.numpy()              # [CO, CI, KW]
+        kw = wq.shape[-1]
+        t_out = oconv.conv_out_length(48, kw, geo["stride"], geo["padding"], geo["dilation"], tr)
+        acc = oconv.gather_conv_codes(xq, wq, fmt, stride=geo["stride"], padding=geo["padding"],
+                                      dilation=geo["dilation"], transpose=tr, t_out=t_out).astype(np.float32)
+        ref = ((acc * s_in).astype(np.float32) * state[key + ".weight_scale"].numpy()[None, :, None]).astype(np.float32)
+        ref = (ref + state[key[:-7] + ".bias"].numpy()[None, :, None]).astype(np.float32)
+        assert y.shape == ref.shape
+        assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < 1e-5, role
