@@ -71,15 +71,48 @@ def gemm_bytes(m, n, k, out_kind):
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock, power and clock-event reasons of one GPU while the timed steps run.
+
+    NVML is read in-process from a thread every 10 ms (no start-up delay, so a short
+    timed region still gets tens of samples); without NVML, ``nvidia-smi -lms 50``.
+    Read-only: nothing here changes a GPU setting."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASON_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                   ("sw_power_cap", 0x4))
+    PERIOD_S = 0.010
 
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.proc = None
+        self.thread = None
+        self.rows = []          # (sm_mhz, max_sm_mhz, reasons mask) per NVML sample
+        self.out = ""
+
+    def _nvml_loop(self, nvml, handle, stop):
+        get_reasons = getattr(nvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        mx = nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM)
+        while not stop.is_set():
+            try:
+                self.rows.append((nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM), mx, get_reasons(handle)))
+            except Exception:
+                pass
+            stop.wait(self.PERIOD_S)
 
     def __enter__(self):
+        import threading
+        try:
+            import pynvml as nvml
+            nvml.nvmlInit()
+            handle = nvml.nvmlDeviceGetHandleByIndex(self.gpu_index)
+            self._stop = threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nvml, handle, self._stop), daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-i", str(self.gpu_index), "-lms", "50"],
@@ -89,7 +122,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -99,6 +134,11 @@ class ClockSampler:
         return False
 
     def summary(self):
+        if self.rows:
+            sm = [float(r[0]) for r in self.rows]
+            reasons = sorted({name for r in self.rows for name, bit in self.REASON_BITS if r[2] & bit})
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(max(r[1] for r in self.rows)),
+                    "reasons": reasons, "samples": len(self.rows), "source": "nvml, 10 ms"}
         rows = [r for r in csv.reader(io.StringIO(self.out or "")) if len(r) >= 9]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
@@ -107,7 +147,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if "Active" == r[5 + i].strip()})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi, 50 ms"}
 
 
 # ---------------------------------------------------------------------------
