@@ -2,8 +2,8 @@
 """Benchmark of the B200 quantized-linear hot path (one JSON line on rank 0).
 
 Headline workload: a Zipformer-style FM acoustic stack of
-12 W8A8 static-E4M3 layers at batch 64 x 760 frames (M = 48640 tokens),
-hidden 512.  One step = one pass of the stack over one batch:
+12 W8A8 static-E4M3 layers on one batch of 64 utterances x 760 frames
+(M = 48640 tokens), hidden 512.  One step = one pass of the stack over the batch:
 
   per layer:  a   = norm_quant(x)                     RMSNorm -> E4M3        [M, 512]
               3x  h = gemm(a,  W_ff_in)  -> E4M3 requant                     [M, 1536]
@@ -13,14 +13,21 @@ hidden 512.  One step = one pass of the stack over one batch:
               c1  = gemm(a,  W_conv1)    -> E4M3 requant                     [M, 1024]
               x'  = gemm(c1, W_conv2)    -> BF16 (next layer's input)        [M, 512]
 
-metric = GEMM TFLOP/s of the whole step (2*M*N*K summed over the 120 GEMMs);
-norm-quant and FIR GB/s are reported under "components".  Data are seeded
+metric = GEMM TFLOP/s of the whole step (2*M*N*K summed over the 120 GEMMs).
+"components" time the other configurations on the same ranks: config 2's
+norm-quant (GB/s), config 3's NVFP4 gated-up and down, config 4's INT8 decode and
+prefill, config 5's FIR (both shapes, B128 as B64 micro-batches), each with its
+roofline fraction and the clocks sampled while it ran.  Data are seeded
 synthetic tensors with BASELINE's shapes and distributions.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-Multi-GPU: launched by torchrun, one rank per GPU, each rank runs its own
-B64x760 batch (weak scaling, no collective on the data path).
-"""
+Multi-GPU: launched by torchrun, one rank per GPU.  The batch is split
+contiguously by utterance (rank r runs utterances [64 r / N, 64 (r + 1) / N), i.e.
+M = 48640 / N rows at N = 1/2/4/8; config 5's B128 becomes 128 / N per GPU);
+weights are replicated and the static scales are calibrated on the whole batch
+(max over the ranks' shards), so the ranks' outputs are exactly the slices of the
+single-GPU result.  No collective on the data path: a barrier and the
+max-reduction of the timings only.  "scaling" is "strong" (fixed total work).
 from __future__ import annotations
 
 import argparse
@@ -37,7 +44,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-M_TOKENS = 64 * 760
+UTTERANCES, FRAMES = 64, 760
+M_TOKENS = UTTERANCES * FRAMES
 HIDDEN = 512
 LAYERS = 12
 # (name, N, K, input buffer, output kind)
@@ -154,19 +162,30 @@ class ClockSampler:
 # the cfg-2 stack on the GPU, as prepared C-ABI calls
 # ---------------------------------------------------------------------------
 class Stack:
-    def __init__(self, device, seed, m=M_TOKENS, layers=LAYERS):
+    """Config 2's stack on rows [rows[0], rows[1]) of the seeded B64x760 batch.
+
+    Every rank draws the same whole batch and the same weights, then keeps its row
+    slice.  Static scales are amax / 448 of each quantized GEMM input over the whole
+    batch: each rank measures its slice and ``reduce_max`` (the max over ranks) makes
+    them equal everywhere, so a rank computes exactly its slice of the single-GPU
+    result.  ``scales`` (from ``calibrated_scales()``) skips the calibration."""
+
+    def __init__(self, device, seed=1234, rows=(0, M_TOKENS), layers=LAYERS, reduce_max=None, scales=None):
         import torch
 
         from inspark_proper_format_b200 import _lib
         self.torch = torch
         self.lib = _lib.load()
         self._lib = _lib
+        self.rows = rows
+        m = rows[1] - rows[0]
         self.m, self.layers, self.device = m, layers, device
         g = torch.Generator(device=device).manual_seed(seed)
-        x = torch.randn(m, HIDDEN, device=device, generator=g)
+        x = torch.randn(M_TOKENS, HIDDEN, device=device, generator=g)          # the whole batch
         out_ch = torch.randperm(HIDDEN, device=device, generator=g)[:5]            # 1% outlier channels x10
         x[:, out_ch] *= 10
-        self.x0 = x.bfloat16()
+        self.x0 = x[rows[0]:rows[1]].bfloat16().contiguous()
+        del x
         bf = torch.bfloat16
         self.buf = {
             "x_in": self.x0.clone(),                                                  # step input (never written)
@@ -190,7 +209,11 @@ class Stack:
                 gemms[name] = dict(w=codes, ws=ws.contiguous(), bias=bias.contiguous(), n=n, k=k)
             self.params.append(dict(gamma=gamma.contiguous(), gemms=gemms))
         self.stream = torch.cuda.current_stream(device).cuda_stream
-        self._calibrate()
+        self.reduce_max = reduce_max or (lambda v: v)
+        self._calibrate(scales)
+
+    def calibrated_scales(self):
+        return [{k: v for k, v in p.items() if k == "a_scale" or k.startswith("scale_")} for p in self.params]
 
     # --- prepared launches -------------------------------------------------
     def _nq_call(self, x, layer):
@@ -229,28 +252,32 @@ class Stack:
         x_in = b["x_in"] if layer == 0 else b["x"][(layer - 1) % 2]
         return x_in, b["x"][layer % 2]
 
-    def _calibrate(self):
-        """Seeded static calibration: activation amax/448 of every quantized GEMM input."""
+    def _calibrate(self, scales=None):
+        """Static calibration: amax / 448 of every quantized GEMM input over the whole
+        batch (this rank's slice, then the max over ranks), layer by layer."""
         torch = self.torch
         b = self.buf
         for layer in range(self.layers):
             p = self.params[layer]
             x_in, x_out = self._io(layer)
-            xf = x_in.float()
-            normed = (xf * torch.rsqrt(torch.mean(xf * xf, dim=-1, keepdim=True) + 1e-6)).bfloat16() * p["gamma"]
-            p["a_scale"] = float(normed.abs().amax()) / 448.0
-            fn, args, _ = self._nq_call(x_in, layer)
-            self._lib.check(fn(*args), "calibration norm_quant")
-            for name, n, k, src, out_kind in LAYER_GEMMS:
-                if out_kind != "e4m3":
-                    continue
-                q = p["gemms"][name]
-                probe = torch.empty(self.m, n, device=self.device, dtype=torch.float32)
-                from inspark_proper_format_b200.gemm import scaled_gemm
-                scaled_gemm(b["a"], q["w"], a_scale=p["a_scale"], w_scale=q["ws"], bias=q["bias"],
-                            out_dtype=torch.float32, out=probe)
-                key = "scale_" + ("h" if name.startswith("ff") else "c1") + name[:3]
-                p[key] = max(float(probe.abs().amax()) / 448.0, 1e-12)
+            if scales is not None:
+                p.update(scales[layer])
+            else:
+                xf = x_in.float()
+                normed = (xf * torch.rsqrt(torch.mean(xf * xf, dim=-1, keepdim=True) + 1e-6)).bfloat16() * p["gamma"]
+                p["a_scale"] = self.reduce_max(float(normed.abs().amax())) / 448.0
+                fn, args, _ = self._nq_call(x_in, layer)
+                self._lib.check(fn(*args), "calibration norm_quant")
+                for name, n, k, src, out_kind in LAYER_GEMMS:
+                    if out_kind != "e4m3":
+                        continue
+                    q = p["gemms"][name]
+                    probe = torch.empty(self.m, n, device=self.device, dtype=torch.float32)
+                    from inspark_proper_format_b200.gemm import scaled_gemm
+                    scaled_gemm(b["a"], q["w"], a_scale=p["a_scale"], w_scale=q["ws"], bias=q["bias"],
+                                out_dtype=torch.float32, out=probe)
+                    key = "scale_" + ("h" if name.startswith("ff") else "c1") + name[:3]
+                    p[key] = max(self.reduce_max(float(probe.abs().amax())) / 448.0, 1e-12)
             # produce this layer's output (the next layer's calibration input)
             for fn, args, _ in self._layer_calls(layer, x_in, x_out):
                 self._lib.check(fn(*args), "calibration step")

@@ -84,6 +84,14 @@ int isp_device_check(void);
    synchronizes `stream`. */
 int isp_read_device_error(int *error_out, int clear, isp_stream_t stream);
 
+/* Self-test of the bounded-wait path (a library diagnostic; the reference has no
+   device-side waits to bound): launches one CTA that holds TMEM, waits on a
+   barrier nothing arrives on for limit_ns nanoseconds (1e3 .. 1e8), records
+   ISP_ERR_TIMEOUT in the device error word, unwinds its other roles through the
+   abort flag and frees TMEM, exactly as a GEMM whose wait expires.  Returns the
+   launch status; the timeout is read back with isp_read_device_error. */
+int isp_wait_selftest(int64_t limit_ns, isp_stream_t stream);
+
 /*
  * Fused row normalization -> quantization.
  *
@@ -268,6 +276,29 @@ int isp_gated_up(const void *A, const void *W1, const void *W3, int interleaved,
                  float out_scale, void *out, int out_dtype, isp_stream_t stream);
 
 /*
+ * INT8 nonlinear-value projection: three INT8 GEMMs sharing one activation,
+ *   z_j[m, n] = acc_j[m, n] * (a_scale * w_scale[jN + n]) + bias[jN + n],
+ *   acc_j = sum_k Q[m, k] * W[jN + n, k] (exact int32), j = 0, 1, 2,
+ * stored as value = tanhf(z0) * z1 and gate = z2 (every step one FP32 rounding,
+ * in the reference's order; tanhf is CUDA's, the function libdevice.tanh calls).
+ *
+ * Replaces: int8_nonlinear_value (Triton, TensorRT plugin
+ *   zipvoice_int8_b*::OriginalInt8NonlinearValue*)
+ *   ops/tensorrt/zipvoice/a1007/b1/int8_nonlinear_value_runtime_kernel.py:6-34,
+ *   ops/tensorrt/zipvoice/a1007/b1/int8_nonlinear_value_plugin.py:7-35
+ *
+ * Q: [M, K] int8 codes, rows m = t * groups + b (the plugin's [T, B, K]).
+ * W: [3N, K] int8 (the three projections stacked, the exported [1152, 512]).
+ * w_scale, bias: [3N] FP32; a_scale > 0 (the per-tensor input scale AS).
+ * value: [groups, M / groups, N] FP32 (row (b, t) = input row t * groups + b);
+ * gate: [M, N] FP32.  N % 16 == 0, K % 16 == 0, M % groups == 0; every pointer
+ * 16-byte aligned.
+ */
+int isp_int8_nonlinear_value(const void *Q, const void *W, int64_t M, int N, int K, int groups,
+                             float a_scale, const float *w_scale, const float *bias,
+                             float *value, float *gate, isp_stream_t stream);
+
+/*
  * NVFP4 block-scaled GEMM on tcgen05 tensor cores (kind::mxf4nvf4, 16-element
  * K blocks, E4M3 block scales):
  *   v[m, n] = alpha * sum_k (e2m1(A[m,k]) sa[m,k/16]) (e2m1(W[n,k]) sw[n,k/16])
@@ -330,6 +361,8 @@ int isp_nvfp4_gated_up(const void *A, const void *A_sf, const void *W13, const v
  *     8192 floats (32 KB), held by every GPU that loads the library until exit.
  *   - The first call on each device resolves the array's address on that device
  *     (device must be current); make that first call before any stream capture.
+ *     The address is cached per device: after cudaDeviceReset the library must be
+ *     reloaded before this entry point is called again.
  *   - The maxima are cleared at the start of each call.  One array per process and
  *     device: calls that overlap in time (other streams, other threads) race on it
  *     and must be serialized by the caller.

@@ -26,6 +26,7 @@ SIGNATURES = {
     "isp_status_string": (ctypes.c_char_p, [_i]),
     "isp_device_check": (_i, []),
     "isp_read_device_error": (_i, [ctypes.POINTER(_i), _i, _vp]),
+    "isp_wait_selftest": (_i, [_i64, _vp]),
     "isp_norm_quant": (_i, [_vp, _i, _i64, _i, _vp, _vp, _f, _f, _i, _i, _f, _vp, _vp, _vp, _vp]),
     "isp_adaln_quant": (_i, [_vp, _i, _i64, _i, _vp, _f, _vp, _vp, _i64, _i, _f, _vp, _vp, _vp, _vp]),
     "isp_conv1d_geometry": (_i, [_i, _i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
@@ -38,6 +39,7 @@ SIGNATURES = {
     "isp_fir_snake": (_i, [_vp, _i64, _i, _i64, _vp, _vp, _vp, _vp, _vp, _i, _vp, _f, _vp]),
     "isp_scaled_gemm": (_i, [_vp, _vp, _i, _i64, _i, _i, _f, _vp, _vp, _vp, _vp, _i, _vp, _i, _f, _vp, _f, _vp]),
     "isp_gated_up": (_i, [_vp, _vp, _vp, _i, _i64, _i, _i, _vp, _vp, _f, _vp, _i, _vp]),
+    "isp_int8_nonlinear_value": (_i, [_vp, _vp, _i64, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _vp]),
     "isp_nvfp4_scales_to_mma": (_i, [_vp, _i64, _i, _vp, _vp]),
     "isp_nvfp4_gemm": (_i, [_vp, _vp, _vp, _vp, _i64, _i, _i, _f, _vp, _vp, _i, _vp, _i, _vp]),
     "isp_nvfp4_gated_up": (_i, [_vp, _vp, _vp, _vp, _i64, _i, _i, _f, _f, _f, _vp, _vp, _vp]),

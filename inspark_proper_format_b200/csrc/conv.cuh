@@ -22,7 +22,10 @@ namespace isp {
 // ---- per-utterance amax ------------------------------------------------------
 // grid (blocks_per_utterance, B); amax[b] must start at +0 (the host clears it).
 // Non-negative floats order like their bit patterns, so an unsigned atomicMax
-// on the bits is the float maximum.
+// on the bits is the float maximum.  fmaxf drops NaN operands, as the reference's
+// tl.max does (Triton's default maxnum semantics, ops/triton/fp8_conv.py:10,15-16):
+// NaN inputs leave the utterance's scale finite and propagate only through their
+// own codes.
 template <bool kBf16>
 __global__ void __launch_bounds__(256) conv_amax_kernel(const void* x, int64_t per_utt, float* amax) {
   const int64_t base = static_cast<int64_t>(blockIdx.y) * per_utt;

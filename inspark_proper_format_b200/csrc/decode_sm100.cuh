@@ -148,8 +148,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       __syncwarp();
       if (++stage == kDecStages) { stage = 0; phase ^= 1u; }
     }
-    for (int s = 0; s < kDecStages; ++s)
-      if (armed[s]) wait_warp(&full_bar[s], armed_phase[s], abort_flag);
+    for (int s = 0; s < kDecStages; ++s)            // in-flight loads land before the CTA exits
+      if (armed[s]) wait_warp_drain(&full_bar[s], armed_phase[s]);
   } else if (warp == 1 && run) {
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc = instr_desc<kInt8 ? AB_I8 : AB_E4M3, kDecBN>();
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
     if (lane == 0) mma_commit(tfull_bar);    // also the drain: arrives once every issued MMA completed
     __syncwarp();
-    wait_warp(tfull_bar, 0, abort_flag);
+    wait_warp_drain(tfull_bar, 0);           // (also on abort: TMEM is freed only after it)
   } else if (warp >= 2 && run) {
     // ------------------------------------------------ TMEM -> shared partial
     const int quarter = warp & 3;

@@ -23,7 +23,9 @@
 // quarters) right before the four K = 64 MMAs that read them.
 // Every mbarrier wait is bounded (~1 s); on expiry the waiting thread records
 // ISP_ERR_TIMEOUT in g_device_error, raises the CTA abort flag, and all roles
-// unwind to the common exit, which drains in-flight TMA/MMA work and frees TMEM.
+// unwind to the common exit.  The producer and MMA warps first wait (ignoring the
+// flag, bounded by their own limit) for the loads and MMAs they issued; then TMEM
+// is freed.
 #pragma once
 
 #include "common.cuh"
@@ -54,7 +56,12 @@ enum AbKind { AB_E4M3 = 0, AB_I8 = 1, AB_FP4 = 2 };
 // phase rows of one utterance, A gathered per (window slot, 128-channel) block from
 // channels-last codes; column co * P + r is output channel co at phase r; output
 // stored transposed to [B, CO, T_out]).
-enum EpiKind { EPI_SCALE = 0, EPI_SWIGLU_PAIRED = 1, EPI_SWIGLU_INTERLEAVED = 2, EPI_CONV = 3 };
+// EPI_NLV: the INT8 nonlinear-value projection: one tile = 64 outputs x 3 stacked
+// projections (B rows [0, 64) = W[n0 ..], [64, 128) = W[N + n0 ..], [128, 192) =
+// W[2N + n0 ..]); z_j = acc_j * (AS * WS[jN + n]) + bias[jN + n], stored as
+// value = tanh(z0) * z1 (rows re-ordered from (t, b) to (b, t)) and gate = z2.
+enum EpiKind { EPI_SCALE = 0, EPI_SWIGLU_PAIRED = 1, EPI_SWIGLU_INTERLEAVED = 2, EPI_CONV = 3, EPI_NLV = 4 };
+constexpr int kNlvBN = 192;   // EPI_NLV tile: 3 x 64 accumulator columns
 // OUT_NVFP4: packed E2M1 codes + E4M3 block scales in the tensor-core layout.
 enum OutKind { OUT_BF16 = 0, OUT_F16 = 1, OUT_F32 = 2, OUT_E4M3 = 3, OUT_NVFP4 = 4 };
 
@@ -110,6 +117,9 @@ struct Params {
   int conv_tab[kConvTab];
   // Streaming scale epilogue: run the last partial wave as half-N tiles (two per tile)
   int tail_split;
+  // EPI_NLV: gate output [M, N] (FP32; value goes to `out`), rows per time step
+  float* nlv_gate;
+  int nlv_groups;
 };
 
 // Shared-memory layout.  Streaming (kBStatK == 0): stage s = [A | B | A scales | B scales].
@@ -169,14 +179,15 @@ ISP_D bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait: true on success; false after the time limit or when another
 // role of this CTA has already given up (abort flag).
-ISP_D bool wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+ISP_D bool wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                        uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer() - start > kWaitLimitNs) {
+      if (globaltimer() - start > limit_ns) {
         record_timeout();
         *abort_flag = 1;
         return false;
@@ -188,7 +199,7 @@ ISP_D bool wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag
 // Bounded wait for a converged warp: every lane polls, lane 0's result decides,
 // and the warp leaves together (a lone polling lane whose warp-mates are parked
 // at a block barrier throttles the tcgen05 issue stream it feeds).
-ISP_D bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+ISP_D bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint64_t limit_ns = kWaitLimitNs) {
   if (__shfl_sync(0xffffffffu, static_cast<int>(mbar_try_wait(bar, parity)), 0)) return true;
   const uint64_t start = globaltimer();
   for (uint32_t i = 1;; ++i) {
@@ -198,11 +209,31 @@ ISP_D bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
       if ((threadIdx.x & 31) == 0) {
         if (*abort_flag) {
           stop = 1;
-        } else if (globaltimer() - start > kWaitLimitNs) {
+        } else if (globaltimer() - start > limit_ns) {
           record_timeout();
           *abort_flag = 1;
           stop = 1;
         }
+      }
+      if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+    }
+  }
+}
+
+// Drain wait for a converged warp.  In-flight TMA copies and issued tcgen05 MMAs
+// complete on their own, so a CTA that is unwinding must still wait for them
+// before it retires or frees TMEM: this wait ignores the abort flag and gives up
+// only after its own time limit (recording ISP_ERR_TIMEOUT).
+ISP_D bool wait_warp_drain(uint64_t* bar, uint32_t parity) {
+  if (__shfl_sync(0xffffffffu, static_cast<int>(mbar_try_wait(bar, parity)), 0)) return true;
+  const uint64_t start = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (__shfl_sync(0xffffffffu, static_cast<int>(mbar_try_wait(bar, parity)), 0)) return true;
+    if ((i & 63u) == 0) {
+      int stop = 0;
+      if ((threadIdx.x & 31) == 0 && globaltimer() - start > kWaitLimitNs) {
+        record_timeout();
+        stop = 1;
       }
       if (__shfl_sync(0xffffffffu, stop, 0)) return false;
     }
@@ -494,6 +525,7 @@ ISP_D void lds32(const float* p, float (&v)[32]) {   // uniform address: a broad
 //   EPI_SCALE:              [0, BN) w_scale (1 when absent), [256, 256 + BN) bias (0 when absent)
 //   EPI_SWIGLU_PAIRED:      [0, 128) s1, [128, 256) s3
 //   EPI_SWIGLU_INTERLEAVED: [0, 256) S[2 n0 ...] (gate, up alternating)
+//   EPI_NLV:                [64 j, 64 j + 64) AS * WS[jN + n], [256 + 64 j, ...) bias[jN + n]
 // Columns at or past N read as 0, so the math needs no column guards.
 // For EPI_SCALE with a per-tensor activation scale the staged column scale is
 // already sa * w_scale[n] (the product the INT8 reference forms as AS * WS[n]).
@@ -518,6 +550,14 @@ struct TileParams {
       } else if constexpr (kEpi == EPI_SWIGLU_PAIRED) {
         const int n = n0 + (i & 127);
         if (n < p.N) x = __ldg((i < 128 ? p.w_scale : p.w_scale2) + n);
+      } else if constexpr (kEpi == EPI_NLV) {
+        // [64 j, 64 j + 64): projection j's AS * WS and bias of the tile's 64 outputs
+        const int n = n0 + (i & 63);
+        if (i < kNlvBN && n < p.N) {
+          const int64_t c = static_cast<int64_t>(i >> 6) * p.N + n;
+          x = __fmul_rn(p.a_scale, __ldg(p.w_scale + c));
+          y = __ldg(p.bias + c);
+        }
       } else {
         if (n0 + (i >> 1) < p.N) x = __ldg(p.w_scale + 2 * n0 + i);
       }
@@ -779,7 +819,9 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
   static_assert(!kFp4 || kBN == 128, "NVFP4 tiles are 128 x 128 (one scale chunk per operand and K = 64)");
   static_assert(kOut != OUT_NVFP4 || (kFp4 && kEpi == EPI_SWIGLU_PAIRED), "NVFP4 output is the FP4 SwiGLU epilogue");
   static_assert(kBStatK % kBK == 0, "resident K is whole 128-byte blocks");
-  using L = Smem<kBN, kStages, kEpiWarps, kFp4, kOut != OUT_NVFP4, kBStatK>;
+  static_assert(kEpi != EPI_NLV || (kBN == kNlvBN && kAB == AB_I8 && kOut == OUT_F32 && kEpiWarps == 8),
+                "nonlinear-value tiles: INT8, 3 x 64 columns, FP32 outputs, two epilogue warps per lane quarter");
+  using L = Smem<kBN, kStages, kEpiWarps, kFp4, kOut != OUT_NVFP4 && kEpi != EPI_NLV, kBStatK>;
   using R = Roles<kEpiWarps>;
   using S = Schedule<kStat>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -806,7 +848,8 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
   // TMEM: two accumulators (columns [0, 2 kBN)); NVFP4 adds its scale columns after
   // them: streaming 32 per stage (A 16, B 16); B-stationary the resident B scales
   // (4 per 64-element K chunk) and 16 A columns per stage.
-  constexpr int kTmemCols = kFp4 ? 512 : 2 * kBN;
+  // (allocations are powers of two: two 192-column nonlinear-value accumulators take 512)
+  constexpr int kTmemCols = (kFp4 || kEpi == EPI_NLV) ? 512 : 2 * kBN;
   constexpr int kSfbResCols = kStat ? (2 * kBStatK / 64) * 4 : 0;
   static_assert(!kFp4 || 2 * kBN + kSfbResCols + (kStat ? 16 : 32) * kStages <= 512, "TMEM columns");
 
@@ -873,6 +916,9 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
               if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
                 tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * (kBN / 2));
                 tma_load_2d(dst + (kBN / 2) * kBK, &tm_b2, bfull_bar, kb * kBK, nt * (kBN / 2));
+              } else if constexpr (kEpi == EPI_NLV) {
+                for (int j = 0; j < 3; ++j)
+                  tma_load_2d(dst + j * (kBN / 3) * kBK, &tm_b, bfull_bar, kb * kBK, j * p.N + nt * (kBN / 3));
               } else {
                 tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * kBN);
               }
@@ -914,6 +960,9 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
               if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
                 tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * (kBN / 2));
                 tma_load_2d(sb + (kBN / 2) * kBK, &tm_b2, &full_bar[stage], kb * kBK, nt * (kBN / 2));
+              } else if constexpr (kEpi == EPI_NLV) {
+                for (int j = 0; j < 3; ++j)
+                  tma_load_2d(sb + j * (kBN / 3) * kBK, &tm_b, &full_bar[stage], kb * kBK, j * p.N + nt * (kBN / 3));
               } else {
                 tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * kBN);
               }
@@ -927,10 +976,11 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
       }
-      // Drain: every armed stage's last load (and the last resident B) has landed before the CTA exits.
+      // Drain: every armed stage's last load (and the last resident B) has landed before
+      // the CTA exits, also when another role gave up (a copy in flight still lands).
       for (int s = 0; s < kStages; ++s)
-        if (armed[s]) wait_warp(&full_bar[s], armed_phase[s], abort_flag);
-      if (kStat && nloads > 0) wait_warp(bfull_bar, (nloads - 1) & 1u, abort_flag);
+        if (armed[s]) wait_warp_drain(&full_bar[s], armed_phase[s]);
+      if (kStat && nloads > 0) wait_warp_drain(bfull_bar, (nloads - 1) & 1u);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -1016,11 +1066,11 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         __syncwarp();
         if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
-      // Drain: all issued MMAs have completed before TMEM is released.
+      // Drain: all issued MMAs have completed before TMEM is released (also on abort).
       if (issued) {
         if (lane == 0) mma_commit(drain_bar);
         __syncwarp();
-        wait_warp(drain_bar, 0, abort_flag);
+        wait_warp_drain(drain_bar, 0);
       }
     }
   } else {
@@ -1028,7 +1078,82 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     const int ew = warp - kEpiWarp0;             // 0 .. kEpiWarps-1
     const int et = threadIdx.x - kEpiWarp0 * 32; // 0 .. kEpiThreads-1
     const int quarter = warp & 3;                // TMEM lane quarter this warp may access
-    if constexpr (kOut == OUT_NVFP4) {
+    if constexpr (kEpi == EPI_NLV) {
+      // 8 warps: TMEM lane quarter x 32-column half of the tile's 64 outputs.  Each
+      // thread owns one row: z0, z1, z2 of its 32 outputs, value = tanh(z0) * z1 to
+      // row (b, t) of [groups, M / groups, N], gate = z2 to row m of [M, N].
+      const int half = ew >> 2;
+      const int row_in_tile = quarter * 32 + lane;
+      const int64_t steps = p.M / p.nlv_groups;   // T: rows are m = t * groups + b
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      TileParams<kEpi, kBN, R::kEpiThreads> tp;
+      if (sched.begin < sched.end) {
+        int mt, nt, hn;
+        sched.coords(p, sched.begin, mt, nt, hn);
+        tp.fetch(p, nt * (kBN / 3), et);
+      }
+      for (int t = sched.begin; t < sched.end; t += sched.step) {
+        int mt, nt, hn;
+        sched.coords(p, t, mt, nt, hn);
+        epilogue_sync<R::kEpiThreads>();
+        tp.store(params, et);
+        epilogue_sync<R::kEpiThreads>();
+        if (t + sched.step < sched.end) {
+          int mt2, nt2, hn2;
+          sched.coords(p, t + sched.step, mt2, nt2, hn2);
+          tp.fetch(p, nt2 * (kBN / 3), et);
+        }
+        if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+        uint32_t z0[32], z1[32], z2[32];
+        tmem_ld32(t_row + half * 32, z0);
+        tmem_ld32(t_row + kBN / 3 + half * 32, z1);
+        tmem_ld32(t_row + 2 * (kBN / 3) + half * 32, z2);
+        tmem_ld_wait(z0, z1);
+        asm volatile("" : "+r"(z2[0]), "+r"(z2[1]), "+r"(z2[2]), "+r"(z2[3]), "+r"(z2[4]), "+r"(z2[5]), "+r"(z2[6]),
+                     "+r"(z2[7]), "+r"(z2[8]), "+r"(z2[9]), "+r"(z2[10]), "+r"(z2[11]), "+r"(z2[12]), "+r"(z2[13]),
+                     "+r"(z2[14]), "+r"(z2[15]), "+r"(z2[16]), "+r"(z2[17]), "+r"(z2[18]), "+r"(z2[19]), "+r"(z2[20]),
+                     "+r"(z2[21]), "+r"(z2[22]), "+r"(z2[23]), "+r"(z2[24]), "+r"(z2[25]), "+r"(z2[26]), "+r"(z2[27]),
+                     "+r"(z2[28]), "+r"(z2[29]), "+r"(z2[30]), "+r"(z2[31]));
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        const int m = mt * kBM + row_in_tile;
+        if (m >= p.M) continue;
+        const int c0 = half * 32;
+        const int n = nt * (kBN / 3) + c0;
+        // z = acc * (AS * WS) + bias (separate roundings: int8_nonlinear_value_runtime_kernel.py:26-28)
+        float v[32], gz[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float a0 = __fadd_rn(__fmul_rn(acc_value<true>(z0[j]), params[c0 + j]), params[256 + c0 + j]);
+          const float a1 = __fadd_rn(__fmul_rn(acc_value<true>(z1[j]), params[64 + c0 + j]), params[320 + c0 + j]);
+          gz[j] = __fadd_rn(__fmul_rn(acc_value<true>(z2[j]), params[128 + c0 + j]), params[384 + c0 + j]);
+          v[j] = __fmul_rn(tanhf(a0), a1);
+        }
+        const int64_t b = m % p.nlv_groups;
+        const int64_t ts = m / p.nlv_groups;
+        float* vrow = static_cast<float*>(p.out) + (b * steps + ts) * p.N + n;
+        float* grow = p.nlv_gate + static_cast<int64_t>(m) * p.N + n;
+        if (n + 32 <= p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            *reinterpret_cast<float4*>(vrow + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            *reinterpret_cast<float4*>(grow + j) = make_float4(gz[j], gz[j + 1], gz[j + 2], gz[j + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n + j < p.N) {
+              vrow[j] = v[j];
+              grow[j] = gz[j];
+            }
+        }
+      }
+    } else if constexpr (kOut == OUT_NVFP4) {
       // 16 warps: TMEM lane quarter x 16-column block of the tile's 64 outputs;
       // each thread quantizes one NVFP4 block (16 outputs) of its row per tile.
       static_assert(kOut != OUT_NVFP4 || kEpiWarps == 16, "NVFP4 epilogue layout");
@@ -1246,6 +1371,43 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
   }
+}
+
+// Self-test of the bounded-wait unwind path (no data, no global memory but the
+// error word): one CTA of three warps, as the GEMM's roles.  Warp 1 holds 32 TMEM
+// columns; warp 0 waits, converged, on an mbarrier that nothing arrives on, with a
+// limit of limit_ns, then records ISP_ERR_TIMEOUT and raises the abort flag; warp 2
+// waits on a second such barrier under the regular 1 s limit and leaves as soon as
+// it sees the flag; TMEM is freed once all three are back.  Every wait ends.
+__global__ void __launch_bounds__(96, 1) wait_selftest_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_word;
+  volatile int* abort_flag = &abort_word;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 32;" ::"r"(smem_u32(&tmem_slot)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  if (warp == 0) {
+    wait_warp(&bars[0], 0, abort_flag, limit_ns);          // expires: records the timeout, raises the flag
+  } else if (warp == 2) {
+    if (threadIdx.x == 64) wait_bounded(&bars[1], 0, abort_flag);   // returns on the flag
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 32;" ::"r"(tmem_base));
 }
 
 }  // namespace gemm

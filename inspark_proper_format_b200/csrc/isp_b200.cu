@@ -2,7 +2,6 @@
 // header is included here so the device error word is shared).
 #include <cudaTypedefs.h>
 
-#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -147,33 +146,31 @@ constexpr int kFp4SwigluEpiWarps = 16;   // one NVFP4 block (16 outputs) per thr
 constexpr int kStatK = 512;
 constexpr int kStatStages = 4;         // FP8 / INT8: 4 x 16 KB of A + 128 KB of B
 constexpr int kFp4StatStages = 6;      // NVFP4: 6 x 18 KB of A (+ scales) + 72 KB of B (+ scales)
+constexpr int kNlvStatStages = 6;      // INT8 nonlinear value: 6 x 16 KB of A + 96 KB of B (3 x 64 rows)
 
-// ISP_GEMM_STREAMING=1 in the environment keeps the streaming schedule (comparisons).
-bool streaming_forced() {
-  static const bool forced = [] {
-    const char* v = getenv("ISP_GEMM_STREAMING");
-    return v != nullptr && v[0] == '1';
-  }();
-  return forced;
-}
-
-// ISP_GEMM_NO_TAIL_SPLIT=1 keeps the last partial wave of streaming GEMMs as whole tiles.
-bool tail_split_disabled() {
-  static const bool off = [] {
-    const char* v = getenv("ISP_GEMM_NO_TAIL_SPLIT");
-    return v != nullptr && v[0] == '1';
-  }();
-  return off;
-}
-
-// ISP_CONV_DIRECT_STORE=1 keeps the convolution epilogue on per-element stores.
-bool conv_direct_forced() {
-  static const bool forced = [] {
-    const char* v = getenv("ISP_CONV_DIRECT_STORE");
-    return v != nullptr && v[0] == '1';
-  }();
-  return forced;
-}
+// Schedule overrides for A/B measurements, fixed at compile time (e.g.
+// -DISP_GEMM_FORCE_STREAMING=1); the shipped library defines none of them, so it
+// has one code path per shape and no run-time switch.
+//   ISP_GEMM_FORCE_STREAMING  stream B through the ring even when K fits the resident tile
+//   ISP_GEMM_NO_TAIL_SPLIT    keep the last partial wave of streaming GEMMs as whole tiles
+//   ISP_CONV_DIRECT_STORE     per-element stores in the convolution epilogue
+//   ISP_GEMM_NO_DECODE        the regular kernel for M <= 128 instead of cluster split-K
+#ifndef ISP_GEMM_FORCE_STREAMING
+#define ISP_GEMM_FORCE_STREAMING 0
+#endif
+#ifndef ISP_GEMM_NO_TAIL_SPLIT
+#define ISP_GEMM_NO_TAIL_SPLIT 0
+#endif
+#ifndef ISP_CONV_DIRECT_STORE
+#define ISP_CONV_DIRECT_STORE 0
+#endif
+#ifndef ISP_GEMM_NO_DECODE
+#define ISP_GEMM_NO_DECODE 0
+#endif
+constexpr bool streaming_forced() { return ISP_GEMM_FORCE_STREAMING != 0; }
+constexpr bool tail_split_disabled() { return ISP_GEMM_NO_TAIL_SPLIT != 0; }
+constexpr bool conv_direct_forced() { return ISP_CONV_DIRECT_STORE != 0; }
+constexpr bool decode_disabled() { return ISP_GEMM_NO_DECODE != 0; }
 
 template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut, int kBStatK = 0>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, const CUtensorMap& o,
@@ -234,16 +231,7 @@ __global__ void scales_to_mma_kernel(const uint32_t* src, int64_t R, int kchunks
   dst[off] = v;
 }
 
-// Small-M path: cluster split-K (decode_sm100.cuh).  ISP_GEMM_NO_DECODE=1 keeps
-// the regular kernel for M <= 128 (comparisons).
-bool decode_disabled() {
-  static const bool off = [] {
-    const char* v = getenv("ISP_GEMM_NO_DECODE");
-    return v != nullptr && v[0] == '1';
-  }();
-  return off;
-}
-
+// Small-M path: cluster split-K (decode_sm100.cuh).
 template <bool kInt8, int kOut>
 int launch_decode(const CUtensorMap& a, const CUtensorMap& b, const Params& p, int splits, int n_tiles,
                   cudaStream_t stream) {
@@ -404,6 +392,13 @@ int isp_read_device_error(int* error_out, int clear, isp_stream_t stream) {
   }
   *error_out = value;
   return ISP_OK;
+}
+
+int isp_wait_selftest(int64_t limit_ns, isp_stream_t stream) {
+  if (limit_ns < 1000 || limit_ns > 100000000) return ISP_ERR_ARG;    // 1 us .. 100 ms
+  if (int st = isp::check_device()) return st;
+  isp::gemm::wait_selftest_kernel<<<1, 96, 0, stream>>>(static_cast<uint64_t>(limit_ns));
+  return isp::launch_status();
 }
 
 int isp_norm_quant(const void* x, int x_dtype, int64_t M, int K, const float* gamma,
@@ -805,6 +800,44 @@ int isp_gated_up(const void* A, const void* W1, const void* W3, int interleaved,
                 : launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_E4M3>(ta, tb, tb2, to, p, stream);
   return stat ? launch<kBN, kSt, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_F32, kStatK>(ta, tb, tb2, to, p, stream)
               : launch<kBN, kStages, kSwigluEpiWarps, AB_E4M3, EPI_SWIGLU_PAIRED, OUT_F32>(ta, tb, tb2, to, p, stream);
+}
+
+int isp_int8_nonlinear_value(const void* Q, const void* W, int64_t M, int N, int K, int groups, float a_scale,
+                             const float* w_scale, const float* bias, float* value, float* gate,
+                             isp_stream_t stream) {
+  using namespace isp::gemm;
+  if (Q == nullptr || W == nullptr || w_scale == nullptr || bias == nullptr || value == nullptr || gate == nullptr)
+    return ISP_ERR_ARG;
+  if (!(a_scale > 0.f) || a_scale == INFINITY) return ISP_ERR_ARG;
+  if (M < 0 || M > 0x7FFFFFFFll || N <= 0 || N % 16 != 0 || N > 0x7FFFFFFF / 3 || K <= 0 || K % 16 != 0 ||
+      groups < 1 || M % groups != 0)
+    return ISP_ERR_SHAPE;
+  if (!isp::aligned16(Q) || !isp::aligned16(W) || !isp::aligned16(w_scale) || !isp::aligned16(bias) ||
+      !isp::aligned16(value) || !isp::aligned16(gate))
+    return ISP_ERR_ALIGN;
+  if (int st = isp::check_device()) return st;
+  if (M == 0) return ISP_OK;
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, Q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, kBK, kBM) ||
+      !make_map(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, 3ull * N, kBK, kNlvBN / 3))
+    return ISP_ERR_ALIGN;
+  Params p{};
+  p.M = static_cast<int>(M);
+  p.N = N;
+  p.K = K;
+  p.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  p.n_tiles = (N + kNlvBN / 3 - 1) / (kNlvBN / 3);
+  p.k_blocks = (K + kBK - 1) / kBK;
+  p.a_scale = a_scale;
+  p.w_scale = w_scale;
+  p.bias = bias;
+  p.out = value;
+  p.nlv_gate = gate;
+  p.nlv_groups = groups;
+  // The output map is unused (direct stores); pass Q's.
+  if (K <= kStatK)
+    return launch<kNlvBN, kNlvStatStages, 8, AB_I8, EPI_NLV, OUT_F32, kStatK>(ta, tb, tb, ta, p, stream);
+  return launch<kNlvBN, kStages, 8, AB_I8, EPI_NLV, OUT_F32>(ta, tb, tb, ta, p, stream);
 }
 
 int isp_nvfp4_scales_to_mma(const void* src, int64_t R, int K, void* dst, isp_stream_t stream) {

@@ -9,7 +9,9 @@ Reference surfaces mirrored here:
   * ``Int8SmoothQuantLinear(original, spec)`` — the INT8 branch of
     ``ExportWeightOp`` (``build/unified_acoustic_export.py:104-112, 160-204``);
   * ``fused_projection_residual``             — ``ops/tensorrt/zipvoice_fp8_b128/b128/residual_kernel.py:4-11``;
-  * ``i8_residual``                           — ``ops/tensorrt/zipvoice/a1007/b1/i8_residual_runtime_kernel.py:5-21``.
+  * ``i8_residual``                           — ``ops/tensorrt/zipvoice/a1007/b1/i8_residual_runtime_kernel.py:5-21``;
+  * ``int8_nonlinear_value``                  — ``ops/tensorrt/zipvoice/a1007/b1/int8_nonlinear_value_runtime_kernel.py:6-34``
+    (plugin contract ``int8_nonlinear_value_plugin.py:7-35``).
 """
 from __future__ import annotations
 
@@ -272,3 +274,29 @@ def i8_residual(q, w, a_scale: float, w_scale, bias, residual):
     """``i8_residual``: ``acc.to(f32) * (AS * WS[n]) + bias + R``, FP32 output."""
     return scaled_gemm(q, w, a_scale=float(a_scale), w_scale=w_scale, bias=bias, residual=residual,
                        out_dtype=torch.float32)
+
+
+def int8_nonlinear_value(q, w, input_scale: float, weight_scale, bias, *, value=None, gate=None):
+    """ZipVoice INT8 nonlinear-attention in_proj with its tanh/value/gate boundary
+    (``zipvoice_int8_b*::OriginalInt8NonlinearValue*``): ``q`` [T, B, K] int8,
+    ``w`` [3N, K] int8 (the three projections stacked), FP32 ``weight_scale`` and
+    ``bias`` [3N], per-tensor ``input_scale``.  ``z_j = acc_j * (AS * WS[jN+n]) +
+    bias[jN+n]``; returns ``value = tanh(z0) * z1`` as [1, B, T, N] and ``gate = z2``
+    as [T, B, N], both FP32 (the plugin's output descriptors)."""
+    if q.dtype != torch.int8 or w.dtype != torch.int8 or q.ndim != 3 or w.ndim != 2:
+        raise ValueError("expected int8 q [T, B, K] and int8 w [3N, K]")
+    steps, groups, k = q.shape
+    if w.shape[1] != k or w.shape[0] % 3:
+        raise ValueError("Input channels differ")
+    n = w.shape[0] // 3
+    weight_scale = _vec(weight_scale.reshape(-1), 3 * n, "weight_scale")
+    bias = _vec(bias.reshape(-1), 3 * n, "bias")
+    if value is None:
+        value = torch.empty(1, groups, steps, n, device=q.device, dtype=torch.float32)
+    if gate is None:
+        gate = torch.empty(steps, groups, n, device=q.device, dtype=torch.float32)
+    status = _lib.load().isp_int8_nonlinear_value(
+        q.contiguous().data_ptr(), w.contiguous().data_ptr(), steps * groups, n, k, groups, float(input_scale),
+        weight_scale.data_ptr(), bias.data_ptr(), value.data_ptr(), gate.data_ptr(), _lib.stream_handle(q.device))
+    _lib.check(status, "isp_int8_nonlinear_value")
+    return value, gate

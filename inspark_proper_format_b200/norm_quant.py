@@ -1,6 +1,6 @@
 """Fused norm -> quantize op (torch-level wrapper over ``isp_norm_quant``).
 
-New op proposed by the survey of the reference: it fuses the reference's
+An op the reference does not have as one call: it fuses the reference's
 separate normalization (RMSNorm / Qwen RMSNorm / BiasNorm) and quantization
 steps (static E4M3 ``_QDQ``, per-row ``_quantize``, INT8 SmoothQuant, NVFP4
 dynamic block quantization) into one memory-bound pass.

@@ -150,9 +150,12 @@ def conv_out_length(t: int, kw: int, stride: int, padding: int, dilation: int, t
 
 
 def dynamic_input_scale(x: np.ndarray) -> np.ndarray:
-    """Per-utterance max(amax / 448, 1e-12) (``ops/triton/fp8_conv.py:6-16``)."""
-    amax = np.abs(np.asarray(x, np.float32)).reshape(x.shape[0], -1).max(axis=1).astype(np.float32)
-    return np.maximum((amax / np.float32(448.0)).astype(np.float32), np.float32(1e-12))
+    """Per-utterance max(amax / 448, 1e-12) (``ops/triton/fp8_conv.py:6-16``).
+    ``tl.max`` and ``tl.maximum`` default to maxnum (NaN operands dropped), so a
+    NaN input leaves its utterance's scale finite (``np.fmax`` semantics)."""
+    a = np.abs(np.asarray(x, np.float32)).reshape(x.shape[0], -1)
+    amax = np.fmax.reduce(np.concatenate([np.zeros((a.shape[0], 1), np.float32), a], axis=1), axis=1)
+    return np.fmax((amax.astype(np.float32) / np.float32(448.0)).astype(np.float32), np.float32(1e-12))
 
 
 def matrix_conv1d(x, packed, scales, bias, ci, co, kw, stride, padding, dilation, transpose, output_padding=0,

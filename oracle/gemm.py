@@ -25,7 +25,9 @@ def fp8_accumulate(a_codes: np.ndarray, w_codes: np.ndarray) -> np.ndarray:
 def int8_accumulate(a_q: np.ndarray, w_q: np.ndarray) -> np.ndarray:
     """Exact int32 accumulator of ``tl.dot(..., out_dtype=int32)``
     (``ops/tensorrt/zipvoice/a1007/b1/i8_residual_runtime_kernel.py:15``)."""
-    return (a_q.astype(np.int64) @ w_q.astype(np.int64).T).astype(np.int32)
+    # float64 products and sums of int8 codes are exact while K * 128 * 128 < 2**53
+    assert a_q.shape[-1] < (1 << 38)
+    return (a_q.astype(np.float64) @ w_q.astype(np.float64).T).astype(np.int32)
 
 
 def scaled_epilogue(acc, a_scale, w_scale, bias=None, residual=None):
@@ -145,3 +147,24 @@ def fp8_linear(x: np.ndarray, packed: np.ndarray, scales: np.ndarray, bias=None,
     w_codes = np.ascontiguousarray(np.asarray(packed, np.uint8)[:, :n].T)
     v = scaled_epilogue(fp8_accumulate(qa, w_codes), sa, scales, bias)
     return bf16_round(v) if out_bf16 else v
+
+
+def int8_nonlinear_value(q, w, a_scale, w_scale, bias, groups=1):
+    """``int8_nonlinear_value`` (``ops/tensorrt/zipvoice/a1007/b1/
+    int8_nonlinear_value_runtime_kernel.py:6-34``): three INT8 projections of one
+    activation, W = [W0; W1; W2] ([3N, K]), exact int32 accumulators,
+    ``z_j = acc_j.to(f32) * (WS[jN + n] * AS) + bias[jN + n]`` (separate roundings,
+    ``enable_fp_fusion=False``), ``value = tanh(z0) * z1``, ``gate = z2``.
+
+    q: [M, K] int8 with rows m = t * groups + b (the plugin's [T, B, K]).
+    Returns value [groups, M // groups, N] (``V[(b * T + t) * N + n]``, :31-33) and
+    gate [M, N] (:34), FP32.  ``np.tanh`` stands in for CUDA's ``tanhf``."""
+    q = np.asarray(q, np.int8).reshape(-1, np.asarray(w).shape[1])
+    n = np.asarray(w).shape[0] // 3
+    acc = int8_accumulate(q, np.asarray(w, np.int8)).astype(np.float32)
+    s = (np.asarray(w_scale, np.float32) * np.float32(a_scale)).astype(np.float32)
+    z = (acc * s[None, :]).astype(np.float32)
+    z = (z + np.asarray(bias, np.float32)[None, :]).astype(np.float32)
+    value = (np.tanh(z[:, :n]).astype(np.float32) * z[:, n:2 * n]).astype(np.float32)
+    steps = q.shape[0] // groups
+    return np.ascontiguousarray(value.reshape(steps, groups, n).transpose(1, 0, 2)), z[:, 2 * n:].copy()

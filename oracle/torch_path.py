@@ -35,7 +35,10 @@ class FP8Layer:
         self.scales = scales
         self.bias = bias
 
-    def __call__(self, x, gamma, eps, norm_scale):
+    def outputs(self, x, gamma, eps, norm_scale):
+        """FP32 outputs of the seven projections whose results leave the layer: the
+        three FF outputs, attention in and out, and the convolution output (the
+        hidden FF / convolution activations pass through their own Q/DQ)."""
         a = qdq_e4m3(rms_norm(x, gamma, eps), norm_scale)
         w = self.weights
         outs = []
@@ -45,4 +48,8 @@ class FP8Layer:
         outs.append(F.linear(a, w[6]))
         outs.append(F.linear(a, w[7]))
         c1 = F.linear(a, w[8])
-        return F.linear(qdq_e4m3(c1, self.scales[3]), w[9]).bfloat16()
+        outs.append(F.linear(qdq_e4m3(c1, self.scales[3]), w[9]))
+        return outs
+
+    def __call__(self, x, gamma, eps, norm_scale):
+        return self.outputs(x, gamma, eps, norm_scale)[-1].bfloat16()

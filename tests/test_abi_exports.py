@@ -54,3 +54,7 @@ def test_host_validation_runs_before_any_device_work(lib):
     # NULL input / bad dtype are rejected on the host, without touching a GPU.
     assert lib.isp_norm_quant(None, 0, 4, 512, None, None, 1e-6, 1.0, 0, 0, 1.0, None, None, None, None) == 7
     assert lib.isp_fir_snake(None, 1, 1, 4, None, None, None, None, None, 1, None, 1.0, None) == 7
+    # limits outside 1 us .. 100 ms are refused before any device access
+    assert lib.isp_wait_selftest(10, None) == 7
+    assert lib.isp_wait_selftest(10**9, None) == 7
+    assert lib.isp_int8_nonlinear_value(None, None, 4, 384, 512, 1, 0.01, None, None, None, None, None) == 7

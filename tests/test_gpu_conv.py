@@ -224,3 +224,22 @@ def test_export_int8_smoothquant_deconv_vs_oracle(C):
     y = q(torch.from_numpy(x).cuda()).cpu().numpy()
     assert y.shape == ref.shape
     assert rel_l2(y, ref) < 1e-6
+
+
+def test_dynamic_conv_nan_input_like_reference(C):
+    """A NaN input element: the reference's ``tl.max`` / ``tl.maximum`` (maxnum)
+    drop it from the utterance's scale, so every other output keeps its value and
+    only outputs whose window covers the NaN are NaN (same NaN mask as the oracle)."""
+    ci, co, kw = 64, 48, 3
+    g = torch.Generator().manual_seed(77)
+    w = torch.randn(co, ci, kw, generator=g) * 0.05
+    packed, scales = og.pack_weight(w.reshape(co, ci * kw).numpy())
+    x = torch.randn(2, ci, 90, generator=g)
+    x[0, 5, 40] = float("nan")
+    y = C.conv1d(x.cuda(), packed_dev(packed), torch.from_numpy(scales).cuda(), None, ci, co, kw, 1, 1, 1, False, 0)
+    ref = oconv.matrix_conv1d(x.numpy(), packed, scales, None, ci, co, kw, 1, 1, 1, False)
+    got = y.cpu().numpy()
+    np.testing.assert_array_equal(np.isnan(got), np.isnan(ref))
+    assert np.isnan(ref).sum() == co * kw                     # 3 output times x every channel of utterance 0
+    ok = ~np.isnan(ref)
+    assert rel_l2(got[ok], ref[ok]) < 1e-6

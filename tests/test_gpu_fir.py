@@ -87,6 +87,22 @@ def test_fir_quant_int8(ops):
     assert np.abs(q.astype(int) - ref.astype(int)).max() <= 1
 
 
+@pytest.mark.parametrize("case", ["a", "b", "c"])
+def test_fir_quant_int8_golden(ops, case):
+    """Against ``deployment/multibatch/fir_quant_kernel.py`` itself (Triton CPU
+    interpreter fixture): log-scale alpha/beta, the INT8 rule, ragged F."""
+    d = np.load(GOLDEN / "fir_quant.npz")
+    q = ops.fir_quant(torch.from_numpy(d[f"{case}_x"]).cuda(), torch.from_numpy(d["up"]).cuda(),
+                      torch.from_numpy(d["down"]).cuda(), torch.from_numpy(d[f"{case}_log_alpha"]).cuda(),
+                      torch.from_numpy(d[f"{case}_log_beta"]).cuda(), torch.from_numpy(d[f"{case}_smooth"]).cuda(),
+                      float(d[f"{case}_scale"][0])).cpu().numpy()
+    ref = d[f"{case}_q"]
+    # the reference divides sin^2 by (beta + 1e-9), the kernel multiplies by the
+    # reciprocal, and the sines differ by ulps: values on an INT8 tie may flip by one
+    assert np.count_nonzero(q != ref) <= max(1, q.size // 10000)
+    assert np.abs(q.astype(int) - ref.astype(int)).max() <= 1
+
+
 def test_fused_alias_free_install_swaps_activation1d(ops):
     class Activation1d(torch.nn.Module):   # same attribute surface as the reference module
         def __init__(self, c):

@@ -301,3 +301,45 @@ def test_residual_dual_output_tail_split(G):
     zref, qref = og.residual_dual(a, w, alpha, bias, r, inv)
     assert rel_l2(y.cpu().numpy(), zref) < 1e-6
     assert np.mean(q.view(torch.uint8).cpu().numpy() != qref) < 1e-3
+
+
+# ---------------------------------------------------------------------------
+# INT8 nonlinear value (three stacked projections, tanh(z0) * z1 and z2)
+# ---------------------------------------------------------------------------
+def _nlv_operands(steps, groups, n, k, seed):
+    g = np.random.default_rng(seed)
+    q = g.integers(-128, 128, (steps, groups, k), dtype=np.int8)
+    w = g.integers(-127, 128, (3 * n, k), dtype=np.int8)
+    ws = (g.random(3 * n) * 2e-3 + 1e-4).astype(np.float32)
+    bias = (g.standard_normal(3 * n) * 0.1).astype(np.float32)
+    return q, w, np.float32(0.011), ws, bias
+
+
+def _nlv_check(value, gate, ref_value, ref_gate):
+    # z = acc * (AS * WS) + bias from an exact int32 accumulator: bit-exact; CUDA's
+    # tanhf and numpy's tanh are each within 2 ulps of tanh, so value within 4 ulps
+    np.testing.assert_array_equal(gate, ref_gate)
+    np.testing.assert_array_max_ulp(value, ref_value, maxulp=4)
+
+
+@pytest.mark.parametrize("case,groups", [("b1", 1), ("b16", 16)])
+def test_int8_nonlinear_value_golden(G, case, groups):
+    d = np.load(GOLDEN / "int8_nonlinear_value.npz")
+    q = torch.from_numpy(d[f"{case}_q"]).cuda()
+    value, gate = G.int8_nonlinear_value(q, torch.from_numpy(d["w"]).cuda(), float(d[f"{case}_as"][0]),
+                                         torch.from_numpy(d[f"{case}_ws"]).cuda(),
+                                         torch.from_numpy(d[f"{case}_bias"]).cuda())
+    assert tuple(value.shape) == d[f"{case}_value"].shape and tuple(gate.shape) == d[f"{case}_gate"].shape
+    _nlv_check(value.cpu().numpy(), gate.cpu().numpy(), d[f"{case}_value"], d[f"{case}_gate"])
+
+
+@pytest.mark.parametrize("steps,groups,n,k", [(300, 1, 384, 512), (37, 8, 80, 512), (200, 1, 128, 1024),
+                                              (5, 3, 16, 48), (760, 64, 384, 512)])
+def test_int8_nonlinear_value_vs_oracle(G, steps, groups, n, k):
+    """Ragged N tiles (80 = 64 + 16), the streaming schedule (K = 1024), tiny
+    shapes, and the config-2 batch (B64 x 760 frames, M = 48640), every row."""
+    q, w, a_s, ws, bias = _nlv_operands(steps, groups, n, k, steps + n + k)
+    value, gate = G.int8_nonlinear_value(torch.from_numpy(q).cuda(), torch.from_numpy(w).cuda(), float(a_s),
+                                         torch.from_numpy(ws).cuda(), torch.from_numpy(bias).cuda())
+    rv, rg = og.int8_nonlinear_value(q.reshape(-1, k), w, a_s, ws, bias, groups)
+    _nlv_check(value[0].cpu().numpy(), gate.reshape(-1, n).cpu().numpy(), rv, rg)

@@ -75,8 +75,12 @@ def test_biasnorm_then_static_e4m3():
     np.testing.assert_allclose(y, d["y"], rtol=2e-6, atol=1e-7)
     codes = normquant.quant_e4m3_static(d["y"], float(d["scale"]))
     np.testing.assert_array_equal(codes, d["codes"])
+    # torch sums the 512 squares in FP32 in its own vectorized order; the oracle (and
+    # the kernel) round the exact sum once.  The normalized values differ by one ulp
+    # in 29 of the 192 rows; not one of the 98304 codes differs.
     mine = normquant.quant_e4m3_static(y, float(d["scale"]))
-    assert np.mean(mine != d["codes"]) < 1e-3
+    assert np.count_nonzero(mine != d["codes"]) == 0
+    assert np.count_nonzero((y != d["y"]).any(axis=1)) <= 32
 
 
 def test_pack_weight_matches_reference():
@@ -211,3 +215,74 @@ def test_fp8_linear_oracle_matches_triton_reference():
     y = gemm.fp8_linear(d["x"], d["packed"], d["scales"], d["bias"], out_bf16=False)
     for split in (1, 3):
         assert rel_l2(y, d[f"y_split{split}"]) < 1e-6
+
+
+@pytest.mark.parametrize("case", ["a", "b", "c"])
+def test_fir_quant_oracle_matches_triton_reference(case):
+    """``deployment/multibatch/fir_quant_kernel.py`` (run by Triton's CPU
+    interpreter: log-scale Snake, FP32 FIR, then the signed INT8 rule
+    ``rint(div_rn(div_rn(y, smooth), scale))``) against ``oracle.fir``."""
+    d = load("fir_quant")
+    alpha = np.exp(d[f"{case}_log_alpha"]).astype(np.float32)
+    inv_beta = (np.float32(1) / (np.exp(d[f"{case}_log_beta"]).astype(np.float32) + np.float32(1e-9))).astype(np.float32)
+    q = fir.alias_free_snake_int8(d[f"{case}_x"], d["up"], d["down"], alpha, inv_beta, d[f"{case}_smooth"],
+                                  float(d[f"{case}_scale"][0]))
+    ref = d[f"{case}_q"]
+    assert q.shape == ref.shape
+    # the kernel divides sin^2 by (beta + 1e-9) where the oracle multiplies by its
+    # reciprocal: FP32 values on an INT8 rounding tie may land on either side
+    assert np.count_nonzero(q != ref) <= max(1, q.size // 10000)
+    assert np.abs(q.astype(int) - ref.astype(int)).max() <= 1
+
+
+@pytest.mark.parametrize("case,groups", [("b1", 1), ("b16", 16)])
+def test_int8_nonlinear_value_oracle_matches_triton_reference(case, groups):
+    """``int8_nonlinear_value`` (b1 and the 16-group variant, run by Triton's CPU
+    interpreter) against ``oracle.gemm.int8_nonlinear_value``: the gate (z2) is
+    bit-exact; value = tanh(z0) * z1 within 2 ulps (both sides use numpy's tanh
+    here; the GPU kernel uses CUDA's tanhf)."""
+    d = load("int8_nonlinear_value")
+    q = d[f"{case}_q"]
+    value, gate = gemm.int8_nonlinear_value(q.reshape(-1, q.shape[-1]), d["w"], float(d[f"{case}_as"][0]),
+                                            d[f"{case}_ws"], d[f"{case}_bias"], groups)
+    np.testing.assert_array_equal(gate, d[f"{case}_gate"].reshape(gate.shape))
+    ref = d[f"{case}_value"].reshape(value.shape)
+    np.testing.assert_array_max_ulp(value, ref, maxulp=2)
+
+
+def test_cpu_reference_arm_is_the_reference_eager_layer():
+    """``oracle/torch_path.FP8Layer`` (the arithmetic ``bench.py --impl reference``
+    times) against the same layer built from the reference's own RMSNorm, _QDQ and
+    FP8 ExportWeightOp modules: all seven layer outputs bit-identical."""
+    import torch
+
+    from oracle.torch_path import FP8Layer
+    d = load("fp8_layer_eager")
+    x = torch.from_numpy(d["x_bits"].view(np.int16)).view(torch.bfloat16)
+    layer = FP8Layer([torch.from_numpy(d[f"wq{i}"]) for i in range(10)],
+                     [torch.tensor(float(v)) for v in d["act_scales"]])
+    outs = layer.outputs(x, torch.from_numpy(d["gamma"]), 1e-6, torch.tensor(float(d["norm_scale"])))
+    for i, o in enumerate(outs):
+        np.testing.assert_array_equal(o.numpy(), d[f"y{i}"], err_msg=f"output {i}")
+    # the weights the bench quantizes itself ((w / s).clamp.to(e4m3) * s) are the folded ones
+    for i in range(10):
+        w = torch.from_numpy(d[f"w{i}"])
+        s = (w.abs().amax(1) / 448).clamp_min(1e-12)
+        wq = (w / s[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).float() * s[:, None]
+        np.testing.assert_array_equal(wq.numpy(), d[f"wq{i}"])
+
+
+def test_fir_torch_f64_matches_activation1d():
+    """The float64 torch restatement the full-size GPU FIR test uses as its
+    reference, against the reference's Activation1d(Snake) outputs."""
+    import torch
+
+    from fir_torch_f64 import activation1d_f64
+    d = load("fir")
+    for t in (1, 2, 5, 12, 301, 1000):
+        x = torch.from_numpy(d[f"x_{t}"])
+        alpha = torch.from_numpy(d["alpha"])
+        ib = torch.from_numpy(fir.snake_inverse_beta(d["alpha"]))
+        y = activation1d_f64(x, torch.from_numpy(d["filter"]), alpha, ib).numpy()
+        assert y.shape == d[f"y_{t}"].shape
+        assert rel_l2(y, d[f"y_{t}"]) < 1e-6, t
