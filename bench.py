@@ -28,6 +28,7 @@ weights are replicated and the static scales are calibrated on the whole batch
 (max over the ranks' shards), so the ranks' outputs are exactly the slices of the
 single-GPU result.  No collective on the data path: a barrier and the
 max-reduction of the timings only.  "scaling" is "strong" (fixed total work).
+"""
 from __future__ import annotations
 
 import argparse
@@ -335,84 +336,63 @@ class Stack:
         return len(self.calls)
 
 
-def fir_component(torch, device, hbm_peak):
-    """cfg-5 BigVGAN FIR, one B64 micro-batch of C=512 x T=16384 (FP32 in + out)."""
-    from inspark_proper_format_b200 import _lib
-    from inspark_proper_format_b200.alias_free import kaiser_sinc_filter, snake_inverse_beta
-    b, c, t = 64, 512, 16384
-    g = torch.Generator(device=device).manual_seed(5)
-    x = torch.randn(b, c, t, device=device, generator=g) * 0.5
-    y = torch.empty_like(x)
-    from inspark_proper_format_b200.alias_free import host_taps
-    up = host_taps(kaiser_sinc_filter())
-    down = host_taps(kaiser_sinc_filter())
-    alpha = torch.rand(c, device=device, generator=g) * 1.5 + 0.5
-    ib = snake_inverse_beta(alpha).contiguous()
-    lib = _lib.load()
-    stream = torch.cuda.current_stream(device).cuda_stream
+# ---------------------------------------------------------------------------
+# single-configuration cases: the bench's components and the --case profiling targets
+# ---------------------------------------------------------------------------
+def _sf_bytes(r, k):
+    return (r + 127) // 128 * 128 * k // 16
+
+
+def _share(units, share):
+    from inspark_proper_format_b200.dp import shard_range
+    rank, world = share
+    a, b = shard_range(units, world, rank)
+    return b - a
+
+
+INT8_SHAPES = [("qkv", 3840, 1280), ("out", 1280, 1280), ("mlp_up", 5120, 1280), ("mlp_down", 1280, 5120)]
+
+
+def build_case(case, torch, device, share=(0, 1), small=False):
+    """Prepared launches of one configuration on this rank's share of its batch
+    (``share`` = (rank, world); split by utterance like the stack).  Returns a dict:
+    fn() enqueues one iteration (an isp status), name, bytes / flops (this rank's
+    algorithmic work per iteration), bound, launches (per iteration), keep (tensors)."""
     import ctypes
-    args = (x.data_ptr(), b * c, c, t, ctypes.addressof(up), ctypes.addressof(down), alpha.data_ptr(), ib.data_ptr(),
-            y.data_ptr(), _lib.F32, None, 0.0, stream)
-    for _ in range(3):
-        _lib.check(lib.isp_fir_snake(*args), "fir")
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)   # cold L2, no host gap in the interval
-    times = []
-    for _ in range(5):
-        flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        lib.isp_fir_snake(*args)
-        e1.record()
-        torch.cuda.synchronize(device)
-        times.append(e0.elapsed_time(e1) / 1e3)
-    sec = statistics.median(times)
-    nbytes = 8 * b * c * t
-    gbs = nbytes / sec / 1e9
-    del x, y, flush
-    return {"workload": "BigVGAN FIR B64xC512xT16384 FP32", "us": round(sec * 1e6, 1), "GB/s": round(gbs, 1),
-            "frac_hbm": round(gbs / hbm_peak, 3), "launches": 1}
 
-
-def run_case(args, torch, device, hbm_peak, bf16_peak):
-    """Single-kernel cases (profiling targets), each timed launch after a 256 MB L2
-    flush: gemm = the dominant cfg-2 projection, norm_quant = cfg-2 norm-quant,
-    fir / fir_c256 = one cfg-5 micro-batch of either shape (B16 with --small), nvfp4_* =
-    config 3, int8_decode / int8_prefill = config 4's projections at M = 64 / 16384,
-    conv / deconv / conv_quant = BigVGAN learned convs."""
     from inspark_proper_format_b200 import _lib
     lib = _lib.load()
     stream = torch.cuda.current_stream(device).cuda_stream
     g = torch.Generator(device=device).manual_seed(0)
-    if args.case == "gemm":
-        m, n, k = M_TOKENS, 1536, 512
-        a = (torch.randn(m, k, device=device, generator=g) * 50).clamp(-448, 448).to(torch.float8_e4m3fn)
-        w = (torch.randn(n, k, device=device, generator=g) * 50).clamp(-448, 448).to(torch.float8_e4m3fn)
-        ws = torch.rand(n, device=device, generator=g) * 1e-4
-        bias = torch.rand(n, device=device, generator=g)
-        out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
-        fn = lib.isp_scaled_gemm
-        fargs = (a.data_ptr(), w.data_ptr(), _lib.E4M3, m, n, k, 0.01, None, ws.data_ptr(), bias.data_ptr(), None,
-                 _lib.F32, out.data_ptr(), _lib.BF16, 1.0, None, 0.0, stream)
-        nbytes, flops = gemm_bytes(m, n, k, "bf16"), 2 * m * n * k
-        name = f"gemm M={m} N={n} K={k} E4M3->BF16"
-    elif args.case == "norm_quant":
-        m, k = M_TOKENS, HIDDEN
-        x = torch.randn(m, k, device=device, generator=g).bfloat16()
-        gamma = torch.rand(k, device=device, generator=g) + 0.5
-        codes = torch.empty(m, k, device=device, dtype=torch.float8_e4m3fn)
-        fn = lib.isp_norm_quant
-        fargs = (x.data_ptr(), _lib.BF16, m, k, gamma.data_ptr(), None, 1e-6, 1.0, _lib.NORM_RMS_GPTFAST,
-                 _lib.Q_E4M3_STATIC, 0.02, None, codes.data_ptr(), None, stream)
-        nbytes, flops = m * k * 3, 0
-        name = f"norm_quant RMSNorm->E4M3 [{m},{k}] BF16"
-    elif args.case == "int8_decode":
-        # config 4 decode: M=64 rows, the AR model's four projections, INT8 SmoothQuant, BF16 out
-        m = 64
-        shapes = [("qkv", 3840, 1280), ("out", 1280, 1280), ("mlp_up", 5120, 1280), ("mlp_down", 1280, 5120)]
-        calls = []
-        nbytes = 0
-        keep = []
-        for _, n, k in shapes:
+    keep = []
+    if case in ("gemm", "norm_quant"):
+        m = _share(UTTERANCES, share) * FRAMES
+        if case == "gemm":
+            n, k = 1536, 512
+            a = (torch.randn(m, k, device=device, generator=g) * 50).clamp(-448, 448).to(torch.float8_e4m3fn)
+            w = (torch.randn(n, k, device=device, generator=g) * 50).clamp(-448, 448).to(torch.float8_e4m3fn)
+            ws = torch.rand(n, device=device, generator=g) * 1e-4
+            bias = torch.rand(n, device=device, generator=g)
+            out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+            keep += [a, w, ws, bias, out]
+            args = (a.data_ptr(), w.data_ptr(), _lib.E4M3, m, n, k, 0.01, None, ws.data_ptr(), bias.data_ptr(), None,
+                    _lib.F32, out.data_ptr(), _lib.BF16, 1.0, None, 0.0, stream)
+            return dict(fn=lambda: lib.isp_scaled_gemm(*args), name=f"cfg2 attn_in gemm M={m} N={n} K={k} E4M3->BF16",
+                        bytes=gemm_bytes(m, n, k, "bf16"), flops=2 * m * n * k, bound="hbm", launches=1, keep=keep)
+        x = torch.randn(m, HIDDEN, device=device, generator=g).bfloat16()
+        gamma = torch.rand(HIDDEN, device=device, generator=g) + 0.5
+        codes = torch.empty(m, HIDDEN, device=device, dtype=torch.float8_e4m3fn)
+        keep += [x, gamma, codes]
+        args = (x.data_ptr(), _lib.BF16, m, HIDDEN, gamma.data_ptr(), None, 1e-6, 1.0, _lib.NORM_RMS_GPTFAST,
+                _lib.Q_E4M3_STATIC, 0.02, None, codes.data_ptr(), None, stream)
+        return dict(fn=lambda: lib.isp_norm_quant(*args), name=f"cfg2 norm_quant RMSNorm->E4M3 [{m},{HIDDEN}] BF16",
+                    bytes=m * HIDDEN * 3, flops=0, bound="hbm", launches=1, keep=keep)
+    if case in ("int8_decode", "int8_prefill"):
+        # config 4: decode = 64 sequences (M = 64), prefill = 64 x 256 tokens; INT8 SmoothQuant
+        # codes through the AR model's four projections, BF16 out, as one CUDA graph
+        m = _share(64, share) * (1 if case == "int8_decode" else 256)
+        calls, nbytes = [], 0
+        for _, n, k in INT8_SHAPES:
             a = torch.randint(-127, 128, (m, k), device=device, generator=g, dtype=torch.int8)
             w = torch.randint(-127, 128, (n, k), device=device, generator=g, dtype=torch.int8)
             ws = torch.rand(n, device=device, generator=g) * 1e-3
@@ -420,95 +400,63 @@ def run_case(args, torch, device, hbm_peak, bf16_peak):
             out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
             keep += [a, w, ws, bias, out]
             calls.append((a.data_ptr(), w.data_ptr(), _lib.I8, m, n, k, 0.01, None, ws.data_ptr(), bias.data_ptr(),
-                          None, _lib.F32, out.data_ptr(), _lib.BF16, 1.0, None, 0.0, stream))
+                          None, _lib.F32, out.data_ptr(), _lib.BF16, 1.0, None, 0.0))
             nbytes += m * k + n * k + m * n * 2 + 8 * n
 
         def launch_all(strm):
             for c in calls:
-                st = lib.isp_scaled_gemm(*c[:-1], strm)
+                st = lib.isp_scaled_gemm(*c, strm)
                 if st:
                     return st
             return 0
-        # decode kernels run for microseconds: replay them as one CUDA graph so the
-        # timing sees device time, not four host-side launches
-        _lib.check(launch_all(stream), args.case)
+        _lib.check(launch_all(stream), case)
         torch.cuda.synchronize(device)
-        graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph()           # four short launches: replay device time, not host calls
         with torch.cuda.graph(graph):
-            _lib.check(launch_all(torch.cuda.current_stream(device).cuda_stream), args.case)
+            _lib.check(launch_all(torch.cuda.current_stream(device).cuda_stream), case)
         keep.append(graph)
 
-        def fn(*_):
+        def replay():
             graph.replay()
             return 0
-        fargs = ()
-        flops = sum(2 * m * n * k for _, n, k in shapes)
-        name = "int8 decode M=64: qkv 1280->3840, out 1280->1280, up 1280->5120, down 5120->1280 (4 launches)"
-    elif args.case == "int8_prefill":
-        # config 4 prefill: M = 64 x 256 tokens through the AR model's four projections,
-        # INT8 SmoothQuant codes, BF16 out, launched back to back
-        m = 64 * 256
-        shapes = [("qkv", 3840, 1280), ("out", 1280, 1280), ("mlp_up", 5120, 1280), ("mlp_down", 1280, 5120)]
-        calls = []
-        nbytes = 0
-        keep = []
-        for _, n, k in shapes:
-            a = torch.randint(-127, 128, (m, k), device=device, generator=g, dtype=torch.int8)
-            w = torch.randint(-127, 128, (n, k), device=device, generator=g, dtype=torch.int8)
-            ws = torch.rand(n, device=device, generator=g) * 1e-3
-            bias = torch.rand(n, device=device, generator=g)
-            out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
-            keep += [a, w, ws, bias, out]
-            calls.append((a.data_ptr(), w.data_ptr(), _lib.I8, m, n, k, 0.01, None, ws.data_ptr(), bias.data_ptr(),
-                          None, _lib.F32, out.data_ptr(), _lib.BF16, 1.0, None, 0.0, stream))
-            nbytes += m * k + n * k + m * n * 2 + 8 * n
-
-        def fn(*_):
-            for c in calls:
-                st = lib.isp_scaled_gemm(*c)
-                if st:
-                    return st
-            return 0
-        fargs = ()
-        flops = sum(2 * m * n * k for _, n, k in shapes)
-        name = "int8 prefill M=16384: qkv 1280->3840, out 1280->1280, up 1280->5120, down 5120->1280 (4 launches)"
-    elif args.case in ("nvfp4_gated_up", "nvfp4_down"):
-        # config 3: gated-up M=51200, K=512, N=2x2048 (NVFP4 h out), down 2048 -> 512 (BF16 out)
-        m = 51200
-        n, k = (2048, 512) if args.case == "nvfp4_gated_up" else (512, 2048)
-        rows_w = 2 * n if args.case == "nvfp4_gated_up" else n
-
-        def sf_bytes(r, kk):
-            return (r + 127) // 128 * 128 * kk // 16
-
+        return dict(fn=replay, name=f"cfg4 int8 {case[5:]} M={m}: qkv 1280->3840, out 1280->1280, up 1280->5120, "
+                                    f"down 5120->1280 (4 launches, one CUDA graph)",
+                    bytes=nbytes, flops=sum(2 * m * n * k for _, n, k in INT8_SHAPES),
+                    bound="hbm" if case == "int8_decode" else "tensor", launches=4, keep=keep, graph=graph)
+    if case in ("nvfp4_gated_up", "nvfp4_down"):
+        # config 3: gated-up M = 64 x 800, K=512, N=2x2048 (NVFP4 h out); down 2048 -> 512 (BF16 out)
+        m = _share(64, share) * 800
+        n, k = (2048, 512) if case == "nvfp4_gated_up" else (512, 2048)
+        rows_w = 2 * n if case == "nvfp4_gated_up" else n
         a = torch.randint(0, 256, (m, k // 2), device=device, generator=g, dtype=torch.uint8)
-        a_sf = torch.randint(0x28, 0x40, (sf_bytes(m, k),), device=device, generator=g, dtype=torch.uint8)
+        a_sf = torch.randint(0x28, 0x40, (_sf_bytes(m, k),), device=device, generator=g, dtype=torch.uint8)
         w = torch.randint(0, 256, (rows_w, k // 2), device=device, generator=g, dtype=torch.uint8)
-        w_sf = torch.randint(0x28, 0x40, (sf_bytes(rows_w, k),), device=device, generator=g, dtype=torch.uint8)
-        if args.case == "nvfp4_gated_up":
+        w_sf = torch.randint(0x28, 0x40, (_sf_bytes(rows_w, k),), device=device, generator=g, dtype=torch.uint8)
+        keep += [a, a_sf, w, w_sf]
+        if case == "nvfp4_gated_up":
             h = torch.empty(m, n // 2, device=device, dtype=torch.uint8)
-            h_sf = torch.empty(sf_bytes(m, n), device=device, dtype=torch.uint8)
-            fn = lib.isp_nvfp4_gated_up
-            fargs = (a.data_ptr(), a_sf.data_ptr(), w.data_ptr(), w_sf.data_ptr(), m, n, k, 1e-3, 1e-3, 0.01,
-                     h.data_ptr(), h_sf.data_ptr(), stream)
-            nbytes = m * k // 2 + sf_bytes(m, k) + rows_w * k // 2 + m * n // 2 + sf_bytes(m, n)
-            flops = 2 * m * rows_w * k
-            name = f"nvfp4 gated-up M={m} N=2x{n} K={k} -> NVFP4 h"
-        else:
-            out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
-            fn = lib.isp_nvfp4_gemm
-            fargs = (a.data_ptr(), a_sf.data_ptr(), w.data_ptr(), w_sf.data_ptr(), m, n, k, 1e-3, None, None,
-                     _lib.F32, out.data_ptr(), _lib.BF16, stream)
-            nbytes = m * k // 2 + sf_bytes(m, k) + rows_w * k // 2 + m * n * 2
-            flops = 2 * m * n * k
-            name = f"nvfp4 gemm M={m} N={n} K={k} -> BF16"
-    elif args.case in ("conv", "deconv", "conv_quant"):
-        # BigVGAN learned convolutions next to the cfg-5 FIR: a resblock Conv1d(512, 512, 3,
-        # dilation 3) at T=16384 and an upsampling ConvTranspose1d(512, 256, 8, stride 4) to
-        # T=16384, B=16, FP32 in/out, dynamic per-utterance E4M3 scale (ops/triton/fp8_conv.py)
+            h_sf = torch.empty(_sf_bytes(m, n), device=device, dtype=torch.uint8)
+            keep += [h, h_sf]
+            args = (a.data_ptr(), a_sf.data_ptr(), w.data_ptr(), w_sf.data_ptr(), m, n, k, 1e-3, 1e-3, 0.01,
+                    h.data_ptr(), h_sf.data_ptr(), stream)
+            return dict(fn=lambda: lib.isp_nvfp4_gated_up(*args), name=f"cfg3 nvfp4 gated-up M={m} N=2x{n} K={k} -> "
+                        f"NVFP4 h", bytes=m * k // 2 + _sf_bytes(m, k) + rows_w * k // 2 + m * n // 2 +
+                        _sf_bytes(m, n), flops=2 * m * rows_w * k, bound="tensor", launches=1, keep=keep, fp4=True)
+        out = torch.empty(m, n, device=device, dtype=torch.bfloat16)
+        keep.append(out)
+        args = (a.data_ptr(), a_sf.data_ptr(), w.data_ptr(), w_sf.data_ptr(), m, n, k, 1e-3, None, None, _lib.F32,
+                out.data_ptr(), _lib.BF16, stream)
+        return dict(fn=lambda: lib.isp_nvfp4_gemm(*args), name=f"cfg3 nvfp4 down M={m} N={n} K={k} -> BF16",
+                    bytes=m * k // 2 + _sf_bytes(m, k) + rows_w * k // 2 + m * n * 2, flops=2 * m * n * k,
+                    bound="tensor", launches=1, keep=keep, fp4=True)
+    if case in ("conv", "deconv", "conv_quant"):
+        # BigVGAN learned convolutions next to the cfg-5 FIR (profiling targets): a resblock
+        # Conv1d(512, 512, 3, dilation 3) at T=16384 and an upsampling ConvTranspose1d(512, 256, 8,
+        # stride 4) to T=16384, B=16, FP32 in/out, dynamic per-utterance E4M3 scale
         from inspark_proper_format_b200 import conv as iconv
+        from inspark_proper_format_b200.gemm import pack_weight
         b = 16
-        if args.case == "deconv":
+        if case == "deconv":
             tr, ci, co, kw, st, pad, dil, t = True, 512, 256, 8, 4, 2, 1, 4096
         else:
             tr, ci, co, kw, st, pad, dil, t = False, 512, 512, 3, 1, 3, 3, 16384
@@ -516,7 +464,6 @@ def run_case(args, torch, device, hbm_peak, bf16_peak):
         w = torch.randn(ci, co, kw, device=device, generator=g) * 0.05 if tr else \
             torch.randn(co, ci, kw, device=device, generator=g) * 0.05
         dense = w.permute(1, 0, 2) if tr else w
-        from inspark_proper_format_b200.gemm import pack_weight
         packed, scales = pack_weight(dense.reshape(co, ci * kw))
         folded = iconv.pack_folded(packed.view(torch.uint8), co, ci, kw, st, dil, pad, tr)
         phases, taps = iconv.geometry(kw, st, dil, pad, tr)
@@ -526,62 +473,128 @@ def run_case(args, torch, device, hbm_peak, bf16_peak):
         amax = torch.empty(b, device=device)
         y = torch.empty(b, co, t_out, device=device)
         bias = torch.rand(co, device=device, generator=g)
+        keep += [x, folded, scales, xq, amax, y, bias]
         qargs = (x.data_ptr(), _lib.F32, b, ci, t, 1, None, 0.0, amax.data_ptr(), _lib.E4M3, xq.data_ptr(), c_pad,
                  stream)
         _lib.check(lib.isp_conv1d_quant(*qargs), "isp_conv1d_quant")
-        if args.case == "conv_quant":
-            fn, fargs = lib.isp_conv1d_quant, qargs
-            nbytes, flops = b * ci * t * 8 + b * t * c_pad, 0     # x read by the amax and the quant pass
-            name = f"conv input amax + quant [{b},{ci},{t}] FP32 -> E4M3 channels-last (3 launches)"
-        else:
-            fn = lib.isp_conv1d
-            fargs = (xq.data_ptr(), _lib.E4M3, b, c_pad, t, folded.data_ptr(), co, kw, st, dil, pad, 0, int(tr), t_out,
-                     0.0, amax.data_ptr(), scales.data_ptr(), bias.data_ptr(), y.data_ptr(), _lib.F32, stream)
-            nbytes = b * t * c_pad + folded.numel() + b * co * t_out * 4
-            flops = 2 * b * t_out * co * ci * (kw // st if tr else kw)     # useful products (no zero taps)
-            kind = f"ConvTranspose1d({ci},{co},{kw},s={st})" if tr else f"Conv1d({ci},{co},{kw},d={dil})"
-            name = f"{kind} B{b} T_in={t} T_out={t_out} E4M3 -> FP32, {phases} folded phase(s) x {taps} window slots"
+        if case == "conv_quant":
+            return dict(fn=lambda: lib.isp_conv1d_quant(*qargs), bytes=b * ci * t * 8 + b * t * c_pad, flops=0,
+                        name=f"conv input amax + quant [{b},{ci},{t}] FP32 -> E4M3 channels-last (3 launches)",
+                        bound="hbm", launches=3, keep=keep)
+        cargs = (xq.data_ptr(), _lib.E4M3, b, c_pad, t, folded.data_ptr(), co, kw, st, dil, pad, 0, int(tr), t_out,
+                 0.0, amax.data_ptr(), scales.data_ptr(), bias.data_ptr(), y.data_ptr(), _lib.F32, stream)
+        kind = f"ConvTranspose1d({ci},{co},{kw},s={st})" if tr else f"Conv1d({ci},{co},{kw},d={dil})"
+        return dict(fn=lambda: lib.isp_conv1d(*cargs), bytes=b * t * c_pad + folded.numel() + b * co * t_out * 4,
+                    flops=2 * b * t_out * co * ci * (kw // st if tr else kw), bound="tensor", launches=1, keep=keep,
+                    name=f"{kind} B{b} T_in={t} T_out={t_out} E4M3 -> FP32, {phases} folded phase(s) x {taps} slots")
+    # config 5 FIR: "fir" / "fir_c256" = one micro-batch of B64 (B16 with small) of either shape;
+    # "fir_b128" / "fir_c256_b128" = this rank's share of the B128 batch in micro-batches of <= 64
+    from inspark_proper_format_b200.alias_free import host_taps, kaiser_sinc_filter, snake_inverse_beta
+    c, t = (256, 65536) if case.startswith("fir_c256") else (512, 16384)
+    if case.endswith("_b128"):
+        utts = _share(128, share)
+        mb = min(64, utts)
     else:
-        import ctypes
+        utts = mb = 16 if small else 64
+    x = torch.randn(mb, c, t, device=device, generator=g) * 0.5
+    y = torch.empty_like(x)
+    taps = host_taps(kaiser_sinc_filter())
+    alpha = torch.rand(c, device=device, generator=g) * 1.5 + 0.5
+    ib = snake_inverse_beta(alpha).contiguous()
+    keep += [x, y, alpha, ib, taps]
+    parts = [min(mb, utts - u) for u in range(0, utts, mb)]
+    fargs = [(x.data_ptr(), p * c, c, t, ctypes.addressof(taps), ctypes.addressof(taps), alpha.data_ptr(),
+              ib.data_ptr(), y.data_ptr(), _lib.F32, None, 0.0, stream) for p in parts]
 
-        from inspark_proper_format_b200.alias_free import host_taps, kaiser_sinc_filter, snake_inverse_beta
-        b = 16 if args.small else 64
-        c, t = (256, 65536) if args.case == "fir_c256" else (512, 16384)   # config 5's two shapes
-        x = torch.randn(b, c, t, device=device, generator=g) * 0.5
-        y = torch.empty_like(x)
-        taps = host_taps(kaiser_sinc_filter())
-        alpha = torch.rand(c, device=device, generator=g) * 1.5 + 0.5
-        ib = snake_inverse_beta(alpha).contiguous()
-        fn = lib.isp_fir_snake
-        fargs = (x.data_ptr(), b * c, c, t, ctypes.addressof(taps), ctypes.addressof(taps), alpha.data_ptr(),
-                 ib.data_ptr(), y.data_ptr(), _lib.F32, None, 0.0, stream)
-        nbytes, flops = 8 * b * c * t, 0
-        name = f"fir B{b}xC{c}xT{t} FP32"
-    for _ in range(args.warmup):
-        _lib.check(fn(*fargs), args.case)
+    def fir_all():
+        for a in fargs:
+            st = lib.isp_fir_snake(*a)
+            if st:
+                return st
+        return 0
+    name = f"cfg5 fir B{utts}xC{c}xT{t} FP32" + (f" as {len(parts)} micro-batch(es) of <= {mb}" if len(parts) > 1
+                                                   else "")
+    return dict(fn=fir_all, name=name, bytes=8 * utts * c * t, flops=0, bound="hbm", launches=len(parts), keep=keep)
+
+
+def time_case(torch, device, c, iters, warmup, flush, ctx=None, gpu_index=0):
+    """Median CUDA-event time of one iteration of case ``c`` (L2 flushed before each
+    timed iteration, outside the events), the slowest rank's median, and the clocks
+    sampled while the timed iterations ran.  Every rank calls this in the same order."""
+    from inspark_proper_format_b200 import _lib
+    for _ in range(warmup):
+        _lib.check(c["fn"](), c["name"])
     torch.cuda.synchronize(device)
-    # a 256 MB write before every timed launch: the launch starts with a cold L2, and the
-    # write keeps the GPU busy while the host enqueues the events and the call, so the
-    # host's call overhead never enters the timed interval
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    if ctx is not None:
+        ctx.barrier()
+    # at least ~60 ms of timed iterations, so the 10 ms clock sampler sees them
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    _lib.check(c["fn"](), c["name"])
+    e1.record()
+    torch.cuda.synchronize(device)
+    est = max(e0.elapsed_time(e1) / 1e3 + 50e-6, 1e-6)                  # + the flush
+    iters = max(iters, min(2000, int(0.06 / est) + 1))
+    if ctx is not None:
+        iters = int(ctx.max_over_ranks(iters, device=device))           # the same count on every rank
     times = []
-    for _ in range(args.steps):
-        flush.zero_()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        fn(*fargs)
-        e1.record()
-        torch.cuda.synchronize(device)
-        times.append(e0.elapsed_time(e1) / 1e3)
+    with ClockSampler(gpu_index) as clk:
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            st = c["fn"]()
+            e1.record()
+            torch.cuda.synchronize(device)
+            _lib.check(st, c["name"])
+            times.append(e0.elapsed_time(e1) / 1e3)
     sec = statistics.median(times)
-    line = {"case": args.case, "kernel": name, "us": round(sec * 1e6, 2), "GB/s": round(nbytes / sec / 1e9, 1),
-            "frac_hbm": round(nbytes / sec / 1e9 / hbm_peak, 3), "launches": args.steps + args.warmup}
-    if flops:
-        line["TFLOP/s"] = round(flops / sec / 1e12, 1)
-        fp4 = args.case.startswith("nvfp4")
-        key = "frac_fp4" if fp4 else ("frac_int8" if args.case.startswith("int8") else "frac_fp8")
-        line[key] = round(flops / sec / 1e12 / ((4 if fp4 else 2) * bf16_peak), 3)   # INT8 dense rate = FP8's
+    slowest = ctx.max_over_ranks(sec, device=device) if ctx is not None else sec
+    return sec, slowest, clk.summary()
+
+
+def case_line(c, sec, hbm_peak, bf16_peak, world=1):
+    """Rates of one case: ``sec`` is the slowest rank's time; every rank's share is
+    the same size (the batches split evenly at N = 1, 2, 4, 8), so the whole job
+    moved world x this rank's bytes and FLOPs."""
+    gbs = c["bytes"] / sec / 1e9
+    line = {"workload": c["name"], "us": round(sec * 1e6, 2), "launches": c["launches"],
+            "GB/s": round(world * gbs, 1), "frac_hbm": round(gbs / hbm_peak, 3)}
+    if c["flops"]:
+        tf = c["flops"] / sec / 1e12
+        mult = 4 if c.get("fp4") else 2                       # FP4 dense = 4x bf16, FP8 / INT8 = 2x
+        line["TFLOP/s"] = round(world * tf, 1)
+        line["frac_fp4" if c.get("fp4") else "frac_fp8_int8"] = round(tf / (mult * bf16_peak), 3)
+    line["bound"] = c["bound"]
+    line["frac"] = line["frac_hbm"] if c["bound"] == "hbm" else line["frac_fp4" if c.get("fp4") else "frac_fp8_int8"]
+    return line
+
+
+def run_case(args, torch, device, hbm_peak, bf16_peak):
+    """--case: time one configuration's kernels alone on one GPU (profiling target)."""
+    c = build_case(args.case, torch, device, small=args.small)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    sec, _, clocks = time_case(torch, device, c, args.steps, args.warmup, flush)
+    line = {"case": args.case, **case_line(c, sec, hbm_peak, bf16_peak), "clocks": clocks}
+    line["kernel"] = line.pop("workload")
     print(json.dumps(line), flush=True)
+
+
+COMPONENTS = ("norm_quant", "nvfp4_gated_up", "nvfp4_down", "int8_decode", "int8_prefill", "fir_b128",
+              "fir_c256_b128")
+
+
+def run_components(torch, device, ctx, hbm_peak, bf16_peak, flush, gpu_index, iters=5, warmup=3):
+    """Every configuration other than the headline, on this rank's share of its batch."""
+    out = {}
+    for case in COMPONENTS:
+        c = build_case(case, torch, device, share=(ctx.rank, ctx.world))
+        _, slowest, clocks = time_case(torch, device, c, iters, warmup, flush, ctx, gpu_index)
+        out[case] = {**case_line(c, slowest, hbm_peak, bf16_peak, ctx.world), "clocks": clocks}
+        del c
+        torch.cuda.empty_cache()
+    return out
+
 
 
 def cpu_sample_layer(m_rows, seed=0):
@@ -642,7 +655,7 @@ def run_reference(args, rank, world):
     value = flops / sec / 1e12
     line = {"metric": "FM-stack GEMM TFLOP/s (B64x760, W8A8 E4M3)", "value": round(value, 4), "unit": "TFLOP/s",
             "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "e4m3", "data": "synthetic",
             "config": {"workload": "cfg2 Zipformer FM layer sample on CPU", "tokens_per_step": m_rows,
                        "layers_per_step": 1},
@@ -662,12 +675,12 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-components", action="store_true")
-    ap.add_argument("--case", choices=("stack", "gemm", "norm_quant", "fir", "nvfp4_gated_up", "nvfp4_down",
-                                       "conv", "deconv", "conv_quant", "int8_prefill", "fir_c256",
-                                       "int8_decode"),
+    ap.add_argument("--case", choices=("stack", "gemm", "norm_quant", "fir", "fir_c256", "fir_b128", "fir_c256_b128",
+                                       "nvfp4_gated_up", "nvfp4_down", "int8_decode", "int8_prefill", "conv",
+                                       "deconv", "conv_quant"),
                     default="stack",
-                    help="stack = the headline step; the others time one kernel (profiling targets)")
-    ap.add_argument("--small", action="store_true", help="smaller FIR case for ncu captures")
+                    help="stack = the headline step; the others time one configuration alone (profiling targets)")
+    ap.add_argument("--small", action="store_true", help="B16 FIR micro-batch for ncu captures")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -680,7 +693,7 @@ def main():
 
     import torch
 
-    from inspark_proper_format_b200.dp import RankContext, weak_scaling_throughput
+    from inspark_proper_format_b200.dp import RankContext, shard_range, strong_scaling_throughput
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     ctx = RankContext(rank, world, local_rank, "nccl").init(timeout_s=300.0, device=device)
@@ -693,48 +706,51 @@ def main():
             run_case(args, torch, device, hbm_peak, bf16_peak)
         ctx.close()
         return
-    stack = Stack(device, seed=1234 + rank)
-    flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)   # > 126 MB L2
-
-    for _ in range(args.warmup):
-        stack.run()
-    torch.cuda.synchronize(device)
-
-    ev = {name: [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True), []]
-          for name in (DOMINANT, "norm_quant")}
-    step_events = []
-    barrier()
-    torch.cuda.synchronize(device)
     gpu_index = local_rank
     if os.environ.get("CUDA_VISIBLE_DEVICES"):
         try:
             gpu_index = int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank])
         except ValueError:
             pass
+    # this rank's utterances of the B64 x 760 batch (contiguous), weights replicated,
+    # static scales calibrated over the whole batch (max over the ranks' shards)
+    u0, u1 = shard_range(UTTERANCES, world, rank)
+    stack = Stack(device, rows=(u0 * FRAMES, u1 * FRAMES),
+                  reduce_max=lambda v: ctx.max_over_ranks(v, device=device))
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=device, dtype=torch.float32)   # > 126 MB L2
+    job_flops = M_TOKENS * FLOPS_PER_TOKEN_LAYER * LAYERS                             # the whole batch per step
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        stack.run()
+    torch.cuda.synchronize(device)
+
+    # Timed region: K steps back to back on one stream, each preceded by a 256 MiB L2
+    # flush inside the region (so every step starts cold and the flushes' ~40 us count),
+    # no event or host sync between launches -- the same launch stream the e2e pass runs.
+    barrier()
+    torch.cuda.synchronize(device)
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(gpu_index) as clocks:
+        e_start.record()
         for _ in range(args.steps):
-            flush.zero_()                                             # untimed L2 flush between steps
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            stack.run()                                               # no per-launch events in timed steps
-            e1.record()
-            step_events.append((e0, e1))
+            flush.zero_()
+            stack.run()
+        e_stop.record()
         torch.cuda.synchronize(device)
     barrier()
-    step_s = [a.elapsed_time(b) / 1e3 for a, b in step_events]
-    total = ctx.max_over_ranks(sum(step_s), device=device)      # the job ends with the slowest rank
+    total = ctx.max_over_ranks(e_start.elapsed_time(e_stop) / 1e3, device=device)   # the slowest rank
     ms_per_step = total / args.steps * 1e3
-    value = weak_scaling_throughput(stack.flops() * args.steps, world, total) / 1e12
+    value = strong_scaling_throughput(job_flops * args.steps, total) / 1e12
 
     # Per-launch timings of the roofline kernel and the norm-quant come from separate,
-    # untimed steps: event records between launches cost ~7% of a step, so they stay
-    # out of the steps that give `value`.
+    # untimed steps: event records between launches cost ~7% of a step.
+    ev = {name: [torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True), []]
+          for name in (DOMINANT, "norm_quant")}
     for _ in range(max(2, min(args.steps, 5))):
         flush.zero_()
         stack.run(events=ev)
     torch.cuda.synchronize(device)
-
-    # dominant kernel roofline (attn_in: 512 -> 1536, BF16 out)
     dom = [a.elapsed_time(b) / 1e3 for a, b in ev[DOMINANT][2]]
     dom_s = sum(dom) / len(dom)
     dom_bytes = gemm_bytes(stack.m, 1536, 512, "bf16")
@@ -746,30 +762,35 @@ def main():
         roof = {"bound": "tensor", "achieved": round(dom_flops / dom_s / 1e12, 1), "peak": fp8_peak, "unit": "TFLOP/s"}
     roof["frac"] = round(roof["achieved"] / roof["peak"], 3)
     roof["traffic"] = None
-    try:   # DRAM read+write per launch from the committed ncu capture of this kernel
+    try:   # DRAM read+write per launch from the committed ncu capture of this kernel (M = 48640)
         with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
-            roof["traffic"] = json.load(f)["gemm_attn_in"]["dram_bytes_per_launch"]
+            t = json.load(f)["gemm_attn_in"]
+        roof["traffic"] = round(t["dram_bytes_per_launch"] * stack.m / t.get("rows", M_TOKENS))
     except (OSError, KeyError, ValueError):
         pass
-    roof["kernel"] = f"gemm {DOMINANT} (M={stack.m}, N=1536, K=512, E4M3 in, BF16 out), {len(dom)} launches"
+    roof["kernel"] = (f"gemm {DOMINANT} (M={stack.m}, N=1536, K=512, E4M3 in, BF16 out), "
+                      f"{len(dom)} launches on rank {rank}")
     roof["us_per_launch"] = round(dom_s * 1e6, 2)
-    roof["peak_source"] = peak_kind + (" (fp8 tensor peak = 2 x measured bf16)" if roof["bound"] == "tensor" else "")
+    roof["peak_source"] = peak_kind + (" (fp8 tensor peak = 2 x measured bf16)" if roof["bound"] == "tensor" else
+                                       " (burst copy bandwidth)")
     nq = [a.elapsed_time(b) / 1e3 for a, b in ev["norm_quant"][2]]
     nq_s = sum(nq) / len(nq)
     nq_bytes = stack.m * HIDDEN * 3
 
-    # end to end through the C ABI: every step uploads its input from pinned host memory
-    # and downloads its result (the stack's output activation) to pinned host memory.
-    # Serving-style pipelining: two input/output buffer sets, uploads and downloads on
-    # their own copy streams, so step i+1's upload and step i-1's download overlap step
-    # i's compute; the timed region runs from before the first upload to after the last
-    # download.
+    # End to end through the C ABI: every step uploads this rank's shard of the input
+    # from pinned host memory and downloads its shard of the result (the stack's output
+    # activation) to pinned host memory.  Serving-style pipelining: two input/output
+    # buffer sets, uploads and downloads on their own copy streams, so step i+1's upload
+    # and step i-1's download overlap step i's compute; the timed region runs from
+    # before the first upload to after the last download and includes the same L2
+    # flush before every step as the device-timed region.
     sets = stack.io_sets(2)
     host_in = stack.x0.cpu().pin_memory()
     host_out = [torch.empty(stack.output.shape, dtype=stack.output.dtype).pin_memory() for _ in sets]
     compute = torch.cuda.current_stream(device)
     up_stream, down_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
     n_e2e = max(3, args.steps // 2)
+    stack_calls_per_step = list(stack.calls)
 
     def e2e_pass(n):
         ev = lambda: torch.cuda.Event(enable_timing=False)  # noqa: E731
@@ -788,7 +809,7 @@ def main():
             compute.wait_event(uploaded[j])
             if downloaded[j] is not None:
                 compute.wait_event(downloaded[j])          # step i-2's result has left this output buffer
-            flush.zero_()                                  # cold L2 for every step, inside the timed region
+            flush.zero_()
             stack.run_calls(sets[j]["calls"], compute.cuda_stream)
             computed[j] = ev()
             computed[j].record(compute)
@@ -807,34 +828,40 @@ def main():
     e2e_pass(2)                                              # warm the copy streams
     torch.cuda.synchronize(device)
     barrier()
-    flush.zero_()
     e2e_total = ctx.max_over_ranks(e2e_pass(n_e2e), device=device)
-    e2e_value = weak_scaling_throughput(stack.flops() * n_e2e, world, e2e_total) / 1e12
+    e2e_value = strong_scaling_throughput(job_flops * n_e2e, e2e_total) / 1e12
     out_ok = bool(torch.equal(host_out[(n_e2e - 1) % 2].to(device), sets[(n_e2e - 1) % 2]["out"]))
+    h2d = host_in.numel() * host_in.element_size()
+    d2h = host_out[0].numel() * host_out[0].element_size()
+    del sets, host_out
 
     components = {
-        "gemm_all": {"TFLOP/s": round(value / world, 1), "frac_fp8_peak": round(value / world / fp8_peak, 3)},
-        "norm_quant": {"workload": f"RMSNorm->E4M3 [{stack.m},{HIDDEN}] BF16 in", "us": round(nq_s * 1e6, 2),
-                       "GB/s": round(nq_bytes / nq_s / 1e9, 1), "frac_hbm": round(nq_bytes / nq_s / 1e9 / hbm_peak, 3)},
+        "gemm_all": {"TFLOP/s": round(value, 1), "frac_fp8_peak": round(value / world / fp8_peak, 3)},
+        "norm_quant_in_stack": {"workload": f"cfg2 RMSNorm->E4M3 [{stack.m},{HIDDEN}] BF16 in, inside the step",
+                                "us": round(nq_s * 1e6, 2), "GB/s": round(world * nq_bytes / nq_s / 1e9, 1),
+                                "frac_hbm": round(nq_bytes / nq_s / 1e9 / hbm_peak, 3)},
     }
-    if not args.no_components and rank == 0:
-        components["fir"] = fir_component(torch, device, hbm_peak)
+    if not args.no_components:
+        del stack
+        torch.cuda.empty_cache()
+        components.update(run_components(torch, device, ctx, hbm_peak, bf16_peak, flush, gpu_index))
 
     line = {
         "metric": "FM-stack GEMM TFLOP/s (B64x760, W8A8 E4M3)", "value": round(value, 2), "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
-        "config": {"workload": "cfg2: Zipformer-style FM stack, 12 W8A8 static-E4M3 layers, M=48640 (B64x760) "
-                               "tokens per GPU, hidden 512, fused RMSNorm->E4M3 + 10 GEMMs per layer",
-                   "tokens_per_gpu": stack.m, "layers": stack.layers, "gemm_flops_per_step": stack.flops(),
-                   "parallelism": f"dp{world} (batch sharded, no collective)",
-                   "l2": "flushed between timed steps (256 MiB write, outside the step events)"},
-        "gpu_launches": stack.launches() * args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
+        "config": {"workload": "cfg2: Zipformer-style FM stack, 12 W8A8 static-E4M3 layers on one batch of "
+                               "B64 x 760 frames (M=48640 tokens), hidden 512, fused RMSNorm->E4M3 + 10 GEMMs per "
+                               "layer; the batch split contiguously by utterance over the GPUs",
+                   "tokens_per_step": M_TOKENS, "tokens_per_gpu": M_TOKENS // world, "layers": LAYERS,
+                   "gemm_flops_per_step": job_flops,
+                   "parallelism": f"dp{world} (utterances split contiguously, weights replicated, no collective)",
+                   "l2": "flushed before every timed step (256 MiB write inside the timed region)"},
+        "gpu_launches": len(stack_calls_per_step) * args.steps,
         "roofline": roof,
         "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",
-                "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
-                "d2h_bytes_per_step": host_out[0].numel() * host_out[0].element_size(),
-                "steps": n_e2e, "result_read_back_ok": out_ok,
+                "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * d2h,
+                "per_gpu_bytes_each_way": h2d, "steps": n_e2e, "result_read_back_ok": out_ok,
                 "mode": "double-buffered: uploads/downloads on copy streams overlap neighbouring steps' compute; "
                         "L2 flushed (256 MiB write) before every step inside the timed region"},
         "clocks": clocks.summary(),

@@ -72,3 +72,10 @@ def weak_scaling_throughput(work_per_rank: float, world: int, slowest_seconds: f
     if slowest_seconds <= 0:
         raise ValueError("elapsed time must be positive")
     return world * work_per_rank / slowest_seconds
+
+
+def strong_scaling_throughput(total_work: float, slowest_seconds: float) -> float:
+    """Whole-job rate of a fixed batch split over the ranks: the job ends with the slowest rank."""
+    if slowest_seconds <= 0:
+        raise ValueError("elapsed time must be positive")
+    return total_work / slowest_seconds

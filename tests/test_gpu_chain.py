@@ -68,3 +68,23 @@ def test_back_to_back_layer_fragment_matches_oracle_stage_by_stage():
     assert rel_l2(y_v, ref_y) < 4e-3                             # BF16 rounding of accumulation-order ulps
     ref_a2, _ = onq.norm_quant(y_v, onq.NORM_RMS_GPTFAST, onq.Q_E4M3_STATIC, gamma=gamma2.numpy(), scale=s_a2)
     np.testing.assert_array_equal(a2_c, ref_a2)
+
+
+def test_bench_stack_shards_are_slices_of_the_full_batch():
+    """The multi-GPU split of ``bench.py``: a rank running utterances [u0, u1) of the
+    B64 x 760 batch with the whole-batch calibration computes exactly rows
+    [760 u0, 760 u1) of the single-GPU output (two layers, bit-exact)."""
+    import bench
+    dev = torch.device("cuda", 0)
+    full = bench.Stack(dev, layers=2)
+    full.run()
+    torch.cuda.synchronize()
+    ref = full.output.clone()
+    scales = full.calibrated_scales()
+    del full
+    for u0, u1 in ((0, 24), (24, 64)):
+        lo, hi = u0 * bench.FRAMES, u1 * bench.FRAMES
+        part = bench.Stack(dev, rows=(lo, hi), layers=2, scales=scales)
+        part.run()
+        torch.cuda.synchronize()
+        assert torch.equal(part.output, ref[lo:hi]), (u0, u1)
