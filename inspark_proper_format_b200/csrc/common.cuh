@@ -49,6 +49,29 @@ inline int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
   return e == cudaSuccess ? ISP_OK : ISP_ERR_LAUNCH;
 }
 
+// launch_pdl for a kernel of thread-block clusters of `cluster` CTAs along x.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              unsigned cluster, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  (void)cudaGetLastError();
+  return e == cudaSuccess ? ISP_OK : ISP_ERR_LAUNCH;
+}
+
 // Device error word (one per device; the library is a single translation unit).
 __device__ int g_device_error = 0;
 

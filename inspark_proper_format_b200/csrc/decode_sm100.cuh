@@ -39,20 +39,7 @@ struct DecSmem {
   static constexpr int kBytes = kBarOffset + 128;
 };
 
-ISP_D uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Every thread of every CTA of the cluster arrives (release) and waits (acquire).
-ISP_D void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-ISP_D uint32_t map_to_rank(uint32_t local_smem_addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
-  return r;
-}
+// cluster_rank, cluster_sync_all and map_to_rank are in gemm_sm100.cuh
 ISP_D uint4 ld_cluster_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -126,7 +113,18 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const bool run = aligned;
-  pdl_wait();      // predecessor complete before any operand or output access
+  // The weight does not depend on the preceding kernel: the producer streams the
+  // weight tiles of its first stages before waiting for it, so this launch's HBM
+  // reads overlap the predecessor's tail; A (its output) is loaded after the wait.
+  const int npre = run ? min(kDecStages, kb1 - kb0) : 0;
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < npre; ++i) {
+      uint8_t* sa = smem + i * L::kStageBytes;
+      mbar_expect_tx(&full_bar[i], L::kStageBytes);
+      tma_load_2d(sa + L::kABytes, &tm_b, &full_bar[i], (kb0 + i) * kBK, n0);
+    }
+  }
+  pdl_wait();      // predecessor complete before any activation or output access
   pdl_trigger();
 
   if (warp == 0 && run) {
@@ -136,14 +134,15 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     bool armed[kDecStages] = {false, false, false, false};
     uint32_t armed_phase[kDecStages] = {0, 0, 0, 0};
     for (int kb = kb0; kb < kb1; ++kb) {
-      if (!wait_warp(&empty_bar[stage], phase ^ 1u, abort_flag)) break;
+      const bool pre = kb - kb0 < npre;       // stage armed and its weight tile issued above
+      if (!pre && !wait_warp(&empty_bar[stage], phase ^ 1u, abort_flag)) break;
       armed[stage] = true;
       armed_phase[stage] = phase;
       if (lane == 0) {
         uint8_t* sa = smem + stage * L::kStageBytes;
-        mbar_expect_tx(&full_bar[stage], L::kStageBytes);
+        if (!pre) mbar_expect_tx(&full_bar[stage], L::kStageBytes);
         tma_load_2d(sa, &tm_a, &full_bar[stage], kb * kBK, 0);
-        tma_load_2d(sa + L::kABytes, &tm_b, &full_bar[stage], kb * kBK, n0);
+        if (!pre) tma_load_2d(sa + L::kABytes, &tm_b, &full_bar[stage], kb * kBK, n0);
       }
       __syncwarp();
       if (++stage == kDecStages) { stage = 0; phase ^= 1u; }

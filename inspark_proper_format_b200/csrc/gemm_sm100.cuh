@@ -37,10 +37,11 @@ constexpr int kBM = 128;
 constexpr int kBK = 128;          // bytes (= elements) of K per stage
 constexpr int kEpiWarp0 = 2;      // warps 0 (TMA) and 1 (MMA) precede the epilogue warps
 
-#ifndef ISP_GEMM_STAGING_BUFS
-#define ISP_GEMM_STAGING_BUFS 1   // 32-row x 128-byte store boxes per epilogue warp
-#endif
-constexpr int kStagingBufs = ISP_GEMM_STAGING_BUFS;
+// 32-row x 128-byte store boxes per epilogue warp: one on a single SM (its shared
+// memory holds the whole B tile), two on SM pairs (half of B per SM), so a warp
+// writes its next box while the previous one is still being read by the TMA store.
+constexpr int kStagingBufsOne = 1;
+constexpr int kStagingBufsPair = 2;
 
 // 4 epilogue warps cover the 4 TMEM lane quarters once; 8 warps take two per
 // quarter, each on half of the tile's columns (twice the latency hiding).
@@ -126,7 +127,7 @@ struct Params {
 // B-stationary (kBStatK > 0 bytes of K): stage s = [A | A scales], then the resident
 // B tile (kBStatK / 128 boxes of kBN rows x 128 B) and its scales, loaded once per
 // N tile.  Scales exist for NVFP4 only; every swizzled region starts 1024-aligned.
-template <int kBN, int kStages, int kEpiWarps, bool kFp4, bool kStaging, int kBStatK>
+template <int kBN, int kStages, int kEpiWarps, bool kFp4, bool kStaging, int kBStatK, int kStagingBufs = kStagingBufsOne>
 struct Smem {
   static constexpr bool kStat = kBStatK > 0;
   static constexpr int kABytes = kBM * kBK;
@@ -307,7 +308,7 @@ ISP_D uint64_t smem_desc_sf(uint32_t addr) {
   return d;
 }
 
-template <int kAB, int kBN>
+template <int kAB, int kBN, int kM = kBM>
 ISP_HD uint32_t instr_desc() {
   if constexpr (kAB == AB_FP4) {
     // Block-scaled descriptor: A/B format E2M1 (1) at bits 7 and 10, scale
@@ -319,7 +320,7 @@ ISP_HD uint32_t instr_desc() {
     // N >> 3 at bit 17, M >> 4 at bit 24.
     constexpr bool kInt8 = kAB == AB_I8;
     return (kInt8 ? (2u << 4) : (1u << 4)) | (kInt8 ? (1u << 7) | (1u << 10) : 0u) |
-           (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+           (static_cast<uint32_t>(kBN >> 3) << 17) | (static_cast<uint32_t>(kM >> 4) << 24);
   }
 }
 
@@ -355,6 +356,68 @@ ISP_D void mma_issue(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t
 ISP_D void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// ---- clusters and the SM-pair (cta_group::2) forms ----
+ISP_D uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster arrives (release) and waits (acquire).
+ISP_D void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+ISP_D uint32_t map_to_rank(uint32_t local_smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier given by its cluster address (this CTA's or the peer's).
+ISP_D void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Arm a barrier given by its cluster address with the bytes this arrive expects.
+ISP_D void mbar_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr), "r"(bytes)
+               : "memory");
+}
+// SM-pair tile load: the box lands in this CTA's shared memory and its bytes are
+// counted on the barrier at `bar_cluster_addr` (the pair leader's), where the MMA
+// that reads both CTAs' halves waits.  No multicast.
+ISP_D void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster_addr, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
+      : "memory");
+}
+// M = 256 MMA over the SM pair (issued by the leader only): A rows [0, 128) and B
+// rows [0, N/2) from the leader's shared memory, A rows [128, 256) and B rows
+// [N/2, N) from the peer's, at the same offsets; each CTA's TMEM receives its 128 rows.
+template <bool kInt8>
+ISP_D void mma_issue_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  if constexpr (kInt8) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  }
+}
+// Commit of the leader's SM-pair MMAs: one arrive on the barrier at this offset in
+// both CTAs of the pair once every MMA issued before it has completed.
+ISP_D void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "{\n .reg .b16 m;\n mov.b16 m, 3;\n"
+      " tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n}" ::"r"(
+          smem_u32(bar))
+      : "memory");
 }
 
 // 32 TMEM lanes x 32 consecutive 32-bit columns -> 32 registers per thread.
@@ -531,6 +594,7 @@ ISP_D void lds32(const float* p, float (&v)[32]) {   // uniform address: a broad
 // already sa * w_scale[n] (the product the INT8 reference forms as AS * WS[n]).
 template <int kEpi, int kBN, int kEpiThreads>
 struct TileParams {
+  static_assert(kEpiThreads <= 256, "one or more entries per epilogue thread");
   static constexpr int kPer = 256 / kEpiThreads;
   float a[kPer], b[kPer];   // entries et + kEpiThreads * h of the 256-wide shared arrays
 
@@ -764,21 +828,22 @@ template <bool kStat>
 struct Schedule {
   int begin, end, step;
   int full;   // streaming with tail_split: units from here on are half-N tiles, two per tile
-  ISP_D Schedule(const Params& p) {
+  // `unit` of `units` workers: the CTA, or the SM pair in the pair schedule
+  ISP_D Schedule(const Params& p, int unit, int units) {
     const int total = p.m_tiles * p.n_tiles;
     full = total;
     if constexpr (kStat) {
-      begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * total / gridDim.x);
-      end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x);
+      begin = static_cast<int>(static_cast<int64_t>(unit) * total / units);
+      end = static_cast<int>(static_cast<int64_t>(unit + 1) * total / units);
       step = 1;
     } else {
-      begin = blockIdx.x;
+      begin = unit;
       end = total;
-      step = gridDim.x;
+      step = units;
       // The last partial wave (rem tiles) would keep rem CTAs busy while the rest idle;
       // as 2 rem half-N tiles it spreads over twice as many CTAs.
-      const int rem = total % static_cast<int>(gridDim.x);
-      if (p.tail_split && rem > 0 && 2 * rem <= static_cast<int>(gridDim.x)) {
+      const int rem = total % units;
+      if (p.tail_split && rem > 0 && 2 * rem <= units) {
         full = total - rem;
         end = total + rem;
       }
@@ -808,7 +873,14 @@ struct Schedule {
 // ----------------------------------------------------------------------------
 // kBStatK > 0: B-stationary schedule holding kBStatK bytes of K of the B tile
 // resident (requires K bytes <= kBStatK).
-template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut, int kBStatK>
+// kPair: SM-pair schedule (a cluster of two CTAs, tcgen05 cta_group::2): 256 x kBN tiles,
+// CTA rank r holds A rows [128 r, 128 r + 128) and B rows [r kBN / 2, (r + 1) kBN / 2) of
+// each tile; the leader (rank 0) issues M = 256 MMAs that read both CTAs' shared memory
+// and write each CTA's 128 rows into its own TMEM; both CTAs run the epilogue of their
+// rows.  The full / bfull / tempty barriers that gate the MMAs live in the leader (TMA
+// bytes of both CTAs and both CTAs' epilogue hand-backs are counted there); the leader's
+// commits arrive on the empty / bempty / tfull / drain barriers of both CTAs.
+template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut, int kBStatK, bool kPair>
 __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_out,
@@ -821,7 +893,12 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
   static_assert(kBStatK % kBK == 0, "resident K is whole 128-byte blocks");
   static_assert(kEpi != EPI_NLV || (kBN == kNlvBN && kAB == AB_I8 && kOut == OUT_F32 && kEpiWarps == 8),
                 "nonlinear-value tiles: INT8, 3 x 64 columns, FP32 outputs, two epilogue warps per lane quarter");
-  using L = Smem<kBN, kStages, kEpiWarps, kFp4, kOut != OUT_NVFP4 && kEpi != EPI_NLV, kBStatK>;
+  static_assert(!kPair || (kStat && kEpi == EPI_SCALE && !kFp4 && kBN == 256),
+                "SM-pair tiles: B-stationary 256 x 256 FP8 / INT8 scale GEMMs");
+  constexpr int kBRows = kPair ? kBN / 2 : kBN;   // B rows in this CTA's shared memory
+  constexpr int kTileM = kPair ? 2 * kBM : kBM;   // rows of one tile
+  constexpr int kStagingBufs = kPair ? kStagingBufsPair : kStagingBufsOne;
+  using L = Smem<kBRows, kStages, kEpiWarps, kFp4, kOut != OUT_NVFP4 && kEpi != EPI_NLV, kBStatK, kStagingBufs>;
   using R = Roles<kEpiWarps>;
   using S = Schedule<kStat>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -860,7 +937,7 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], kEpiWarps);      // one arrive per epilogue warp
+      mbar_init(&tempty_bar[a], kPair ? 2 * kEpiWarps : kEpiWarps);   // one arrive per epilogue warp
     }
     mbar_init(drain_bar, 1);
     mbar_init(bfull_bar, 1);
@@ -873,17 +950,69 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     if constexpr (kOut != OUT_NVFP4) prefetch_tmap(&tm_out);
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (kPair) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // pair: both CTAs' barriers are initialized before either sends a remote arrive or bytes
+  if constexpr (kPair) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const S sched(p);
-  // The prologue above touches no global memory; from here on the kernel reads its
-  // predecessor's outputs, so wait for it, then let the next kernel start early.
+  const uint32_t rank = kPair ? cluster_rank() : 0u;
+  const bool leader = rank == 0;
+  const S sched(p, kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x),
+                kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x));
+  // Resident B tile `nt` (B-stationary): the weight rows of one N tile, all of K.
+  auto load_resident_b = [&](int nt) {
+    uint32_t bytes = static_cast<uint32_t>(p.k_blocks) * L::kBBytes;
+    if constexpr (kFp4) bytes += static_cast<uint32_t>(p.k_chunks) * kSfChunk;
+    if constexpr (kPair) {
+      if (lane == 0 && leader) mbar_expect_tx(bfull_bar, 2 * bytes);      // both halves land on the leader's
+    } else {
+      if (lane == 0) mbar_expect_tx(bfull_bar, bytes);
+    }
+    for (int kb = 0; kb < p.k_blocks && lane == 0; ++kb) {
+      uint8_t* dst = smem + L::kBResOffset + kb * L::kBBytes;
+      if constexpr (kPair) {
+        tma_load_2d_pair(dst, &tm_b, map_to_rank(smem_u32(bfull_bar), 0), kb * kBK,
+                         nt * kBN + static_cast<int>(rank) * kBRows);
+      } else if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
+        tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * (kBN / 2));
+        tma_load_2d(dst + (kBN / 2) * kBK, &tm_b2, bfull_bar, kb * kBK, nt * (kBN / 2));
+      } else if constexpr (kEpi == EPI_NLV) {
+        for (int j = 0; j < 3; ++j)
+          tma_load_2d(dst + j * (kBN / 3) * kBK, &tm_b, bfull_bar, kb * kBK, j * p.N + nt * (kBN / 3));
+      } else {
+        tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * kBN);
+      }
+    }
+    if constexpr (kFp4)
+      if (lane == 0)
+        bulk_load(smem + L::kSfbResOffset, p.sfb + static_cast<int64_t>(nt) * p.k_chunks * kSfChunk,
+                  static_cast<uint32_t>(p.k_chunks) * kSfChunk, bfull_bar);
+  };
+  // The prologue above touches no global memory.  The weight does not depend on the
+  // preceding kernel: the producer loads the first resident B tile before waiting
+  // for it, so that load overlaps the predecessor's tail.  Everything else (A, the
+  // epilogue's parameters, residuals and outputs) waits; then the next kernel may
+  // start its own prologue.
+  int pre_nt = -1;
+  if constexpr (kStat) {
+    if (warp == 0 && sched.begin < sched.end) {
+      int mt0, hn0;
+      sched.coords(p, sched.begin, mt0, pre_nt, hn0);
+      load_resident_b(pre_nt);
+      __syncwarp();
+    }
+  }
   pdl_wait();
   pdl_trigger();
 
@@ -898,35 +1027,17 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
 #pragma unroll
       for (int s = 0; s < kStages; ++s) armed[s] = false, armed_phase[s] = 0;
       bool ok = true;
-      int cur_nt = -1;
-      uint32_t nloads = 0;                       // resident-B loads issued
+      int cur_nt = pre_nt;                       // loaded before the dependency wait
+      uint32_t nloads = pre_nt >= 0 ? 1u : 0u;   // resident-B loads issued
       for (int t = sched.begin; t < sched.end && ok; t += sched.step) {
         int mt, nt, hn;
         sched.coords(p, t, mt, nt, hn);   // a half-N tile loads the whole tile's A and B
-        const int m0 = mt * kBM;
+        const int m0 = mt * kTileM + static_cast<int>(rank) * kBM;
         if constexpr (kStat) {
           if (nt != cur_nt) {
             // reload the resident B tile once every MMA reading the previous one completed
             if (nloads > 0 && !wait_warp(bempty_bar, (nloads - 1) & 1u, abort_flag)) { ok = false; break; }
-            uint32_t bytes = static_cast<uint32_t>(p.k_blocks) * L::kBBytes;
-            if constexpr (kFp4) bytes += static_cast<uint32_t>(p.k_chunks) * kSfChunk;
-            if (lane == 0) mbar_expect_tx(bfull_bar, bytes);
-            for (int kb = 0; kb < p.k_blocks && lane == 0; ++kb) {
-              uint8_t* dst = smem + L::kBResOffset + kb * L::kBBytes;
-              if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
-                tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * (kBN / 2));
-                tma_load_2d(dst + (kBN / 2) * kBK, &tm_b2, bfull_bar, kb * kBK, nt * (kBN / 2));
-              } else if constexpr (kEpi == EPI_NLV) {
-                for (int j = 0; j < 3; ++j)
-                  tma_load_2d(dst + j * (kBN / 3) * kBK, &tm_b, bfull_bar, kb * kBK, j * p.N + nt * (kBN / 3));
-              } else {
-                tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * kBN);
-              }
-            }
-            if constexpr (kFp4)
-              if (lane == 0)
-                bulk_load(smem + L::kSfbResOffset, p.sfb + static_cast<int64_t>(nt) * p.k_chunks * kSfChunk,
-                          static_cast<uint32_t>(p.k_chunks) * kSfChunk, bfull_bar);
+            load_resident_b(nt);
             __syncwarp();
             cur_nt = nt;
             ++nloads;
@@ -941,8 +1052,14 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
             uint32_t bytes = L::kABytes + (kStat ? 0 : L::kBBytes);
             const int nch = kFp4 ? min(4, p.k_chunks - 4 * kb) : 0;   // 64-element scale chunks of this stage
             if constexpr (kFp4) bytes += static_cast<uint32_t>(nch) * kSfChunk * (kStat ? 1 : 2);
-            mbar_expect_tx(&full_bar[stage], bytes);
-            if constexpr (kEpi == EPI_CONV) {
+            if constexpr (kPair) {
+              if (leader) mbar_expect_tx(&full_bar[stage], 2 * bytes);
+              tma_load_2d_pair(sa, &tm_a, map_to_rank(smem_u32(&full_bar[stage]), 0), kb * kBK, m0);
+            } else {
+              mbar_expect_tx(&full_bar[stage], bytes);
+            }
+            if constexpr (kPair) {
+            } else if constexpr (kEpi == EPI_CONV) {
               const int b = mt / p.conv_tpb;
               const int j = kb / p.conv_cblocks;
               const int e = p.conv_tab[j];
@@ -978,15 +1095,23 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
       }
       // Drain: every armed stage's last load (and the last resident B) has landed before
       // the CTA exits, also when another role gave up (a copy in flight still lands).
-      for (int s = 0; s < kStages; ++s)
-        if (armed[s]) wait_warp_drain(&full_bar[s], armed_phase[s]);
-      if (kStat && nloads > 0) wait_warp_drain(bfull_bar, (nloads - 1) & 1u);
+      // (pair: the loads count on the leader's barriers; the peer's warp 1 waits for the
+      // leader's final MMA commit instead, which follows every load the MMAs consumed)
+      if (!kPair || leader) {
+        for (int s = 0; s < kStages; ++s)
+          if (armed[s]) wait_warp_drain(&full_bar[s], armed_phase[s]);
+        if (kStat && nloads > 0) wait_warp_drain(bfull_bar, (nloads - 1) & 1u);
+      }
     }
+  } else if (warp == 1 && kPair && !leader) {
+    // pair peer: no MMAs here; before the CTA may retire, wait for the leader's final
+    // commit (every MMA reading this CTA's shared memory has completed)
+    wait_warp_drain(drain_bar, 0);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     // The whole warp runs the loop (waits converged); lane 0 issues tcgen05 ops.
     {
-      const uint32_t idesc = instr_desc<kAB, kBN>();
+      const uint32_t idesc = instr_desc<kAB, kBN, kTileM>();
       const uint32_t idesc_half = instr_desc<kAB, kBN / 2>();   // half-N tiles of the split tail
       const uint32_t sfb_res_t = tmem_base + static_cast<uint32_t>(2 * kBN);   // B-stationary NVFP4
       int stage = 0;
@@ -1003,7 +1128,10 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         (void)mt;
         if constexpr (kStat) {
           if (nt != cur_nt) {
-            if (cur_nt >= 0 && lane == 0) mma_commit(bempty_bar);   // arrives when every MMA on the old B completed
+            if (cur_nt >= 0 && lane == 0) {   // arrives when every MMA on the old B completed
+              if constexpr (kPair) mma_commit_pair(bempty_bar);
+              else mma_commit(bempty_bar);
+            }
             __syncwarp();
             if (!wait_warp(bfull_bar, bphase, abort_flag)) break;
             bphase ^= 1u;
@@ -1051,24 +1179,35 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
               const uint32_t id = hn >= 0 ? idesc_half : idesc;
 #pragma unroll
               for (int kk = 0; kk < kBK / 32; ++kk) {
-                mma_issue<kInt8>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(bh + kk * 32), id,
-                                 (kb | kk) != 0);
+                if constexpr (kPair)
+                  mma_issue_pair<kInt8>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(bh + kk * 32), id,
+                                        (kb | kk) != 0);
+                else
+                  mma_issue<kInt8>(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(bh + kk * 32), id,
+                                   (kb | kk) != 0);
               }
             }
-            mma_commit(&empty_bar[stage]);
+            if constexpr (kPair) mma_commit_pair(&empty_bar[stage]);
+            else mma_commit(&empty_bar[stage]);
           }
           __syncwarp();
           issued = true;
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        if (lane == 0) mma_commit(&tfull_bar[acc]);
+        if (lane == 0) {
+          if constexpr (kPair) mma_commit_pair(&tfull_bar[acc]);
+          else mma_commit(&tfull_bar[acc]);
+        }
         __syncwarp();
         if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       }
       // Drain: all issued MMAs have completed before TMEM is released (also on abort).
       if (issued) {
-        if (lane == 0) mma_commit(drain_bar);
+        if (lane == 0) {
+          if constexpr (kPair) mma_commit_pair(drain_bar);   // also releases the peer's warp 1
+          else mma_commit(drain_bar);
+        }
         __syncwarp();
         wait_warp_drain(drain_bar, 0);
       }
@@ -1211,7 +1350,7 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
       for (int t = sched.begin; t < sched.end; t += sched.step) {
         int mt, nt, hn;
         sched.coords(p, t, mt, nt, hn);
-        const int m0 = mt * kBM;
+        const int m0 = mt * kTileM + static_cast<int>(rank) * kBM;     // this CTA's 128 rows of the tile
         const int n0 = nt * kOutCols + (hn > 0 ? kOutCols / 2 : 0);   // half-N tile: its columns
         // Per-column parameters of this tile -> shared memory (zero past column N),
         // then start fetching the next tile's.
@@ -1230,7 +1369,10 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
           // warps of the upper columns but handing the accumulator back
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+          if (lane == 0) {
+            if constexpr (kPair) mbar_arrive_cluster(map_to_rank(smem_u32(&tempty_bar[acc]), 0));
+            else mbar_arrive(&tempty_bar[acc]);
+          }
           if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
           continue;
         }
@@ -1261,7 +1403,10 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
             // every column of the accumulator is in registers: hand it back to the MMA warp
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+            if (lane == 0) {
+              if constexpr (kPair) mbar_arrive_cluster(map_to_rank(smem_u32(&tempty_bar[acc]), 0));
+              else mbar_arrive(&tempty_bar[acc]);
+            }
           }
           const int col = (g0 + g) * 32;           // first output column of this group, tile-relative
           const int n = n0 + col;
@@ -1367,9 +1512,15 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // pair: neither CTA retires while the other may still arrive on its barriers or
+  // (leader's MMAs) read its shared memory
+  if constexpr (kPair) cluster_sync_all();
   tc_fence_after();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
+    if constexpr (kPair)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
   }
 }
 

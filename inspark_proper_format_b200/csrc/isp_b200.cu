@@ -66,16 +66,16 @@ EncodeFn encode_fn() {
 
 // 2-D row-major tensor [outer, inner] with a (box_inner x box_outer) box and 128-byte swizzle.
 bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
-              uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+              uint64_t outer, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeFn fn = encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {inner * static_cast<uint64_t>(elem_bytes)};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // 3-D row-major uint8 tensor [d2, d1, d0] (d0 innermost) with a (box0 x box1 x 1) box, 128-byte swizzle.
@@ -120,6 +120,7 @@ bool make_out_map(CUtensorMap* map, void* out, int out_kind, int64_t M, int N) {
                   static_cast<uint32_t>(128 / eb), 32);
 }
 
+
 #ifndef ISP_GEMM_STAGES
 #define ISP_GEMM_STAGES 4
 #endif
@@ -147,6 +148,12 @@ constexpr int kStatK = 512;
 constexpr int kStatStages = 4;         // FP8 / INT8: 4 x 16 KB of A + 128 KB of B
 constexpr int kFp4StatStages = 6;      // NVFP4: 6 x 18 KB of A (+ scales) + 72 KB of B (+ scales)
 constexpr int kNlvStatStages = 6;      // INT8 nonlinear value: 6 x 16 KB of A + 96 KB of B (3 x 64 rows)
+// SM pairs: each CTA holds half of the B tile (64 KB at K = 512), which leaves room for
+// six 16 KB A stages and two staging boxes per epilogue warp.
+#ifndef ISP_GEMM_PAIR_STAGES
+#define ISP_GEMM_PAIR_STAGES 6
+#endif
+constexpr int kPairStages = ISP_GEMM_PAIR_STAGES;
 
 // Schedule overrides for A/B measurements, fixed at compile time (e.g.
 // -DISP_GEMM_FORCE_STREAMING=1); the shipped library defines none of them, so it
@@ -155,6 +162,7 @@ constexpr int kNlvStatStages = 6;      // INT8 nonlinear value: 6 x 16 KB of A +
 //   ISP_GEMM_NO_TAIL_SPLIT    keep the last partial wave of streaming GEMMs as whole tiles
 //   ISP_CONV_DIRECT_STORE     per-element stores in the convolution epilogue
 //   ISP_GEMM_NO_DECODE        the regular kernel for M <= 128 instead of cluster split-K
+//   ISP_GEMM_NO_PAIR          B-stationary scale GEMMs on one CTA per tile instead of SM pairs
 #ifndef ISP_GEMM_FORCE_STREAMING
 #define ISP_GEMM_FORCE_STREAMING 0
 #endif
@@ -167,52 +175,90 @@ constexpr int kNlvStatStages = 6;      // INT8 nonlinear value: 6 x 16 KB of A +
 #ifndef ISP_GEMM_NO_DECODE
 #define ISP_GEMM_NO_DECODE 0
 #endif
+#ifndef ISP_GEMM_NO_PAIR
+#define ISP_GEMM_NO_PAIR 0
+#endif
 constexpr bool streaming_forced() { return ISP_GEMM_FORCE_STREAMING != 0; }
 constexpr bool tail_split_disabled() { return ISP_GEMM_NO_TAIL_SPLIT != 0; }
 constexpr bool conv_direct_forced() { return ISP_CONV_DIRECT_STORE != 0; }
 constexpr bool decode_disabled() { return ISP_GEMM_NO_DECODE != 0; }
+constexpr bool pair_schedule_enabled() { return ISP_GEMM_NO_PAIR == 0; }
 
-template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut, int kBStatK = 0>
+template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut, int kBStatK = 0, bool kPair = false>
 int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, const CUtensorMap& o,
            const Params& p, cudaStream_t stream) {
-  auto kern = gemm_kernel<kBN, kStages, kEpiWarps, kAB, kEpi, kOut, kBStatK>;
-  constexpr int kSmem = Smem<kBN, kStages, kEpiWarps, kAB == AB_FP4, kOut != OUT_NVFP4, kBStatK>::kBytes;
+  auto kern = gemm_kernel<kBN, kStages, kEpiWarps, kAB, kEpi, kOut, kBStatK, kPair>;
+  constexpr int kSmem = Smem<kPair ? kBN / 2 : kBN, kStages, kEpiWarps, kAB == AB_FP4, kOut != OUT_NVFP4 && kEpi != EPI_NLV,
+                             kBStatK, kPair ? kStagingBufsPair : kStagingBufsOne>::kBytes;
   static_assert(kSmem <= 232448, "shared memory budget of one sm_100 CTA");
   static bool configured[64] = {false};
+  static int max_pairs[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
       return ISP_ERR_LAUNCH;
+    if constexpr (kPair) {
+      // persistent pairs: no more clusters than can be resident at once
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (sm_count() / 2));
+      cfg.blockDim = dim3(Roles<kEpiWarps>::kThreads);
+      cfg.dynamicSmemBytes = kSmem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = sm_count() / 2;
+      }
+      max_pairs[dev] = n < sm_count() / 2 ? n : sm_count() / 2;
+    }
     configured[dev] = true;
   }
   const int tiles = p.m_tiles * p.n_tiles;
+  if constexpr (kPair) {
+    const int cap = (dev >= 0 && dev < 64 && max_pairs[dev] > 0) ? max_pairs[dev] : sm_count() / 2;
+    const int pairs = tiles < cap ? tiles : cap;
+    return launch_pdl_cluster(kern, dim3(2 * pairs), dim3(Roles<kEpiWarps>::kThreads), kSmem, stream, 2u, a, b, b2,
+                              o, p);
+  }
   const int grid = tiles < sm_count() ? tiles : sm_count();
   return launch_pdl(kern, dim3(grid), dim3(Roles<kEpiWarps>::kThreads), kSmem, stream, a, b, b2, o, p);
 }
 
+// Schedules: 0 streaming, 1 B-stationary (one CTA per tile), 2 B-stationary SM pairs.
+enum Sched { SCHED_STREAM = 0, SCHED_STAT = 1, SCHED_PAIR = 2 };
+
 template <int kAB, int kOut>
-int launch_scale(bool stat, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const Params& p,
+int launch_scale(int sched, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const Params& p,
                  cudaStream_t s) {
   if constexpr (kAB == AB_FP4) {
-    return stat ? launch<kFp4BN, kFp4StatStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut, kStatK>(a, b, b, o, p, s)
-                : launch<kFp4BN, kFp4Stages, kScaleEpiWarps, kAB, EPI_SCALE, kOut>(a, b, b, o, p, s);
+    return sched != SCHED_STREAM
+               ? launch<kFp4BN, kFp4StatStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut, kStatK>(a, b, b, o, p, s)
+               : launch<kFp4BN, kFp4Stages, kScaleEpiWarps, kAB, EPI_SCALE, kOut>(a, b, b, o, p, s);
   } else {
-    return stat ? launch<kBN, kStatStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut, kStatK>(a, b, b, o, p, s)
-                : launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut>(a, b, b, o, p, s);
+    if (sched == SCHED_PAIR)
+      return launch<kBN, kPairStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut, kStatK, true>(a, b, b, o, p, s);
+    return sched == SCHED_STAT ? launch<kBN, kStatStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut, kStatK>(a, b, b, o, p, s)
+                               : launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut>(a, b, b, o, p, s);
   }
 }
 
 template <int kAB>
-int dispatch_scale_out(int out_kind, bool stat, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
+int dispatch_scale_out(int out_kind, int sched, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o,
                        const Params& p, cudaStream_t s) {
   switch (out_kind) {
-    case OUT_BF16: return launch_scale<kAB, OUT_BF16>(stat, a, b, o, p, s);
-    case OUT_F16: return launch_scale<kAB, OUT_F16>(stat, a, b, o, p, s);
-    case OUT_F32: return launch_scale<kAB, OUT_F32>(stat, a, b, o, p, s);
+    case OUT_BF16: return launch_scale<kAB, OUT_BF16>(sched, a, b, o, p, s);
+    case OUT_F16: return launch_scale<kAB, OUT_F16>(sched, a, b, o, p, s);
+    case OUT_F32: return launch_scale<kAB, OUT_F32>(sched, a, b, o, p, s);
     case OUT_E4M3:
       if constexpr (kAB == AB_FP4) return ISP_ERR_DTYPE;
-      else return launch_scale<kAB, OUT_E4M3>(stat, a, b, o, p, s);
+      else return launch_scale<kAB, OUT_E4M3>(sched, a, b, o, p, s);
     default: return ISP_ERR_DTYPE;
   }
 }
@@ -720,15 +766,19 @@ int isp_scaled_gemm(const void* A, const void* W, int ab_dtype, int64_t M, int N
     return ab_dtype == ISP_I8 ? dispatch_decode<true>(out_kind, ta, tb, p, splits, n_tiles, stream)
                               : dispatch_decode<false>(out_kind, ta, tb, p, splits, n_tiles, stream);
   }
+  // K <= 512 bytes: B-stationary; M > 128 rows on SM pairs (256-row tiles, half of B per SM)
+  const bool stat = K <= kStatK && !streaming_forced();
+  const int sched = !stat ? SCHED_STREAM : (pair_schedule_enabled() ? SCHED_PAIR : SCHED_STAT);
   CUtensorMap ta, tb, to;
   if (!make_map(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, kBK, kBM) ||
-      !make_map(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, kBK, kBN) || !make_out_map(&to, out, out_kind, M, N))
+      !make_map(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, kBK, sched == SCHED_PAIR ? kBN / 2 : kBN) ||
+      !make_out_map(&to, out, out_kind, M, N))
     return ISP_ERR_ALIGN;
   Params p{};
   p.M = static_cast<int>(M);
   p.N = N;
   p.K = K;
-  p.m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  p.m_tiles = static_cast<int>((M + (sched == SCHED_PAIR ? 2 * kBM : kBM) - 1) / (sched == SCHED_PAIR ? 2 * kBM : kBM));
   p.n_tiles = (N + kBN - 1) / kBN;
   p.k_blocks = (K + kBK - 1) / kBK;
   p.a_scale = a_scale;
@@ -740,12 +790,11 @@ int isp_scaled_gemm(const void* A, const void* W, int ab_dtype, int64_t M, int N
   p.out_inv = out_inv_scale;
   p.out2 = out2;
   p.out2_inv = out2_inv_scale;
-  const bool stat = K <= kStatK && !streaming_forced();
   // streaming: the last partial wave runs as half-N tiles (needs the two-warps-per-quarter
   // epilogue, whose upper warps simply hand a half tile's accumulator back)
   p.tail_split = !stat && kScaleEpiWarps == 8 && !tail_split_disabled();
-  return ab_dtype == ISP_I8 ? dispatch_scale_out<AB_I8>(out_kind, stat, ta, tb, to, p, stream)
-                            : dispatch_scale_out<AB_E4M3>(out_kind, stat, ta, tb, to, p, stream);
+  return ab_dtype == ISP_I8 ? dispatch_scale_out<AB_I8>(out_kind, sched, ta, tb, to, p, stream)
+                            : dispatch_scale_out<AB_E4M3>(out_kind, sched, ta, tb, to, p, stream);
 }
 
 int isp_gated_up(const void* A, const void* W1, const void* W3, int interleaved, int64_t M, int N, int K,
@@ -889,7 +938,7 @@ int isp_nvfp4_gemm(const void* A, const void* A_sf, const void* W, const void* W
   p.residual = residual;
   p.residual_f32 = residual_dtype == ISP_F32;
   const bool stat = K / 2 <= kStatK && !streaming_forced();
-  return dispatch_scale_out<AB_FP4>(out_kind, stat, ta, tb, to, p, stream);
+  return dispatch_scale_out<AB_FP4>(out_kind, stat ? SCHED_STAT : SCHED_STREAM, ta, tb, to, p, stream);
 }
 
 int isp_nvfp4_gated_up(const void* A, const void* A_sf, const void* W13, const void* W13_sf, int64_t M, int N, int K,
