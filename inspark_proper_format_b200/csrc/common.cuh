@@ -21,6 +21,8 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // Checks (once per device) that the current device is compute capability 10.x.
 int check_device();
+// Multiprocessor count of the current device (cached per device).
+int sm_count();
 
 // Maps the last CUDA launch error to a status code (clears sticky launch error).
 inline int launch_status() {
@@ -132,6 +134,16 @@ ISP_D float div_rn_recip(float x, float d, float y) {
   const float r = __fmaf_rn(-q0, d, x);
   const float q = __fmaf_rn(r, y, q0);
   return (fabsf(q0) < 0x1p100f && fabsf(d) < 0x1p126f) ? q : q0;
+}
+
+// div_rn_recip on two quotients with one divisor, the three IEEE steps two lanes per
+// instruction (f32x2: each lane rounded exactly as the scalar operation).
+ISP_D float2 div_rn_recip2(float2 x, float d, float y) {
+  const float2 q0 = __fmul2_rn(x, make_float2(y, y));
+  const float2 r = __ffma2_rn(q0, make_float2(-d, -d), x);
+  const float2 q = __ffma2_rn(r, make_float2(y, y), q0);
+  const bool dd = fabsf(d) < 0x1p126f;
+  return make_float2((fabsf(q0.x) < 0x1p100f && dd) ? q.x : q0.x, (fabsf(q0.y) < 0x1p100f && dd) ? q.y : q0.y);
 }
 
 ISP_D int8_t int8_rne_sat(float v) {

@@ -68,30 +68,51 @@ ISP_D float row_max(float v) {
   return v;
 }
 
-// kGroups: max 8-element groups per lane kept in registers (K <= 8 * kLanes * kGroups).
-// A block of 8 warps covers 8 * 32 / kLanes rows; rows past M keep their lanes in
-// the shuffles and skip every load and store.
-template <bool kBF16, int kNorm, int kFmt, int kGroups, int kLanes>
-__global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
-  static_assert(kLanes == 16 || kLanes == 32, "a row spans a half or a whole warp");
-  const int lane = threadIdx.x % kLanes;   // lane within the row
-  const int64_t row = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * (32 / kLanes) +
-                      (threadIdx.x & 31) / kLanes;
-  pdl_wait();       // predecessor's output (this kernel's input) complete and visible
-  pdl_trigger();
-  const bool active = row < p.M;
-  if (__all_sync(0xffffffffu, !active)) return;
-  const int K = p.K;
-  const int ngroups = active ? K >> 3 : 0;   // an inactive row owns no groups
-  const void* xrow = kBF16 ? static_cast<const void*>(static_cast<const uint16_t*>(p.x) + row * K)
-                           : static_cast<const void*>(static_cast<const float*>(p.x) + row * K);
+// One row's input as loaded (BF16: one 16-byte word per 8-element group; FP32: two),
+// kept raw so the next row's loads can be in flight while this row is computed.
+template <bool kBF16>
+struct RawGroup {
+  uint4 w[kBF16 ? 1 : 2];
+};
 
-  float v[kGroups][8];
+template <bool kBF16, int kGroups, int kLanes>
+ISP_D void load_row_raw(const NormQuantParams& p, int64_t row, int lane, RawGroup<kBF16> (&raw)[kGroups]) {
+  if (row >= p.M) return;
+  const int ngroups = p.K >> 3;
 #pragma unroll
   for (int i = 0; i < kGroups; ++i) {
     const int g = lane + kLanes * i;
-    if (g < ngroups) load_group<kBF16>(xrow, g, v[i]);
+    if (g < ngroups) {
+      if constexpr (kBF16) {
+        raw[i].w[0] = ldg_nc_v4(static_cast<const uint16_t*>(p.x) + row * p.K + g * 8);
+      } else {
+        const float* q = static_cast<const float*>(p.x) + row * p.K + g * 8;
+        raw[i].w[0] = ldg_nc_v4(q);
+        raw[i].w[1] = ldg_nc_v4(q + 4);
+      }
+    }
   }
+}
+
+template <bool kBF16>
+ISP_D void unpack_group(const RawGroup<kBF16>& r, float (&v)[8]) {
+  if constexpr (kBF16) {
+    bf16x8_to_f32(r.w[0], v);
+  } else {
+    v[0] = __uint_as_float(r.w[0].x); v[1] = __uint_as_float(r.w[0].y);
+    v[2] = __uint_as_float(r.w[0].z); v[3] = __uint_as_float(r.w[0].w);
+    v[4] = __uint_as_float(r.w[1].x); v[5] = __uint_as_float(r.w[1].y);
+    v[6] = __uint_as_float(r.w[1].z); v[7] = __uint_as_float(r.w[1].w);
+  }
+}
+
+// Normalization and quantization of one row whose values are in v (kLanes lanes;
+// rows past M keep their lanes in the shuffles and skip every load and store).
+template <bool kBF16, int kNorm, int kFmt, int kGroups, int kLanes>
+ISP_D void norm_quant_row(const NormQuantParams& p, int64_t row, int lane, float (&v)[kGroups][8]) {
+  const bool active = row < p.M;
+  const int K = p.K;
+  const int ngroups = active ? K >> 3 : 0;   // an inactive row owns no groups
 
   // ---- normalization ------------------------------------------------------
   if constexpr (kNorm != ISP_NORM_NONE) {
@@ -108,7 +129,12 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
         for (int j = 0; j < 8; ++j) {
           float d = v[i][j];
           if constexpr (kNorm == ISP_NORM_BIAS) d = __fsub_rn(d, b8[j]);
-          acc[j & 3] += static_cast<double>(__fmul_rn(d, d));
+          if constexpr (kBF16 && kNorm != ISP_NORM_BIAS) {
+            // a BF16 value's square is exact in FP32 and in double: one double FMA
+            acc[j & 3] = __fma_rn(static_cast<double>(d), static_cast<double>(d), acc[j & 3]);
+          } else {
+            acc[j & 3] += static_cast<double>(__fmul_rn(d, d));
+          }
         }
       }
     }
@@ -133,13 +159,23 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
           load_param8(p.ada_b + grp * K, g, ab);
         }
         if constexpr (kNorm == ISP_NORM_RMS_GPTFAST && kBF16) {
-          // BF16 rounding of the normalized pair in one conversion
+          // x * r and the product with gamma two elements per instruction (f32x2, each
+          // lane rounded as the scalar op), the BF16 rounding of the pair in one conversion
+          const float2 r2 = make_float2(r, r);
 #pragma unroll
           for (int j = 0; j < 8; j += 2) {
-            const uint32_t h = pack_bf16_rn(__fmul_rn(v[i][j], r), __fmul_rn(v[i][j + 1], r));
-            v[i][j] = __uint_as_float(h << 16);
-            v[i][j + 1] = __uint_as_float(h & 0xFFFF0000u);
+            const float2 t = __fmul2_rn(make_float2(v[i][j], v[i][j + 1]), r2);
+            const uint32_t h = pack_bf16_rn(t.x, t.y);
+            float2 y = __fmul2_rn(make_float2(__uint_as_float(h << 16), __uint_as_float(h & 0xFFFF0000u)),
+                                  make_float2(gm[j], gm[j + 1]));
+            if (p.ada_w != nullptr) {   // scalar: a packed multiply-add may be contracted to one rounding
+              y.x = __fadd_rn(__fmul_rn(aw[j], y.x), ab[j]);
+              y.y = __fadd_rn(__fmul_rn(aw[j + 1], y.y), ab[j + 1]);
+            }
+            v[i][j] = y.x;
+            v[i][j + 1] = y.y;
           }
+          continue;
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -187,9 +223,9 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
         for (int h = 0; h < 2; ++h) {
           const float* q = &v[i][4 * h];
           // satfinite == the reference's clamp(-448, 448) before the cast (NaN stays NaN)
-          uint32_t lo = e4m3x2(div_rn_recip(q[0], s, rs), div_rn_recip(q[1], s, rs));
-          uint32_t hi = e4m3x2(div_rn_recip(q[2], s, rs), div_rn_recip(q[3], s, rs));
-          w[h] = lo | (hi << 16);
+          const float2 a = div_rn_recip2(make_float2(q[0], q[1]), s, rs);
+          const float2 b = div_rn_recip2(make_float2(q[2], q[3]), s, rs);
+          w[h] = static_cast<uint32_t>(e4m3x2(a.x, a.y)) | (static_cast<uint32_t>(e4m3x2(b.x, b.y)) << 16);
         }
         *reinterpret_cast<uint2*>(out + g * 8) = make_uint2(w[0], w[1]);
       }
@@ -255,21 +291,67 @@ __global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
   }
 }
 
+// kGroups: max 8-element groups per lane kept in registers (K <= 8 * kLanes * kGroups).
+// Persistent blocks of 8 warps walk rows with a stride of the whole grid; each row's
+// lanes issue the loads of their next row before normalizing and quantizing the current
+// one, so HBM reads stay in flight while the row is computed.
+template <bool kBF16, int kNorm, int kFmt, int kGroups, int kLanes>
+__global__ void __launch_bounds__(256) norm_quant_kernel(NormQuantParams p) {
+  static_assert(kLanes == 16 || kLanes == 32, "a row spans a half or a whole warp");
+  const int lane = threadIdx.x % kLanes;   // lane within the row
+  constexpr int kRowsPerBlock = 8 * (32 / kLanes);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kRowsPerBlock;
+  int64_t row = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * (32 / kLanes) +
+                (threadIdx.x & 31) / kLanes;
+  pdl_wait();       // predecessor's output (this kernel's input) complete and visible
+  pdl_trigger();
+  if (__all_sync(0xffffffffu, row >= p.M)) return;
+  RawGroup<kBF16> raw[kGroups];
+  load_row_raw<kBF16, kGroups, kLanes>(p, row, lane, raw);
+  for (;;) {
+    float v[kGroups][8];
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) unpack_group<kBF16>(raw[i], v[i]);
+    const int64_t next = row + stride;
+    load_row_raw<kBF16, kGroups, kLanes>(p, next, lane, raw);   // in flight during this row
+    norm_quant_row<kBF16, kNorm, kFmt, kGroups, kLanes>(p, row, lane, v);
+    row = next;
+    if (__all_sync(0xffffffffu, row >= p.M)) break;
+  }
+}
+
+// Persistent grid: as many blocks as are resident at once (at most one per 16 or 8 rows).
+template <typename Kern>
+int launch_norm_quant_persistent(Kern kern, int64_t rows_per_block, const NormQuantParams& p, cudaStream_t stream) {
+  static int per_sm[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int occ = dev >= 0 && dev < 64 ? per_sm[dev] : 0;
+  if (occ == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 256, 0) != cudaSuccess || occ < 1) {
+      cudaGetLastError();
+      occ = 1;
+    }
+    if (dev >= 0 && dev < 64) per_sm[dev] = occ;
+  }
+  const int64_t need = (p.M + rows_per_block - 1) / rows_per_block;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * occ;
+  return launch_pdl(kern, dim3(static_cast<unsigned>(need < cap ? need : cap)), dim3(256), 0, stream, p);
+}
+
 template <bool kBF16, int kNorm, int kFmt>
 int launch_norm_quant_groups(const NormQuantParams& p, cudaStream_t stream) {
-  const dim3 block(256);
   if (p.K <= 512) {   // half-warp rows: 16 rows per block, up to 4 groups per lane
-    const dim3 grid(static_cast<unsigned>((p.M + 15) / 16));
-    if (p.K <= 256) return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 2, 16>, grid, block, 0, stream, p);
-    return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 4, 16>, grid, block, 0, stream, p);
+    if (p.K <= 256) return launch_norm_quant_persistent(norm_quant_kernel<kBF16, kNorm, kFmt, 2, 16>, 16, p, stream);
+    return launch_norm_quant_persistent(norm_quant_kernel<kBF16, kNorm, kFmt, 4, 16>, 16, p, stream);
   }
   const int per_lane = (p.K / 8 + 31) / 32;
-  const dim3 grid(static_cast<unsigned>((p.M + 7) / 8));
-  if (per_lane <= 4) return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 4, 32>, grid, block, 0, stream, p);
-  if (per_lane <= 8) return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 8, 32>, grid, block, 0, stream, p);
-  if (per_lane <= 16) return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 16, 32>, grid, block, 0, stream, p);
+  if (per_lane <= 4) return launch_norm_quant_persistent(norm_quant_kernel<kBF16, kNorm, kFmt, 4, 32>, 8, p, stream);
+  if (per_lane <= 8) return launch_norm_quant_persistent(norm_quant_kernel<kBF16, kNorm, kFmt, 8, 32>, 8, p, stream);
+  if (per_lane <= 16) return launch_norm_quant_persistent(norm_quant_kernel<kBF16, kNorm, kFmt, 16, 32>, 8, p, stream);
   if constexpr (kNorm == ISP_NORM_NONE) {
-    if (per_lane <= 32) return launch_pdl(norm_quant_kernel<kBF16, kNorm, kFmt, 32, 32>, grid, block, 0, stream, p);
+    if (per_lane <= 32)
+      return launch_norm_quant_persistent(norm_quant_kernel<kBF16, kNorm, kFmt, 32, 32>, 8, p, stream);
   }
   return ISP_ERR_SHAPE;
 }
