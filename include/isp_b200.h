@@ -14,10 +14,12 @@
  * dependent launch, so a kernel may start while the preceding kernel of this
  * library on the same stream finishes.  Before waiting for it, a GEMM or
  * convolution reads only its weight operand (W / W13 / w_packed and NVFP4 weight
- * scales); every activation, scale, bias, residual and output is touched only
- * after the preceding kernel has completed.  A weight must therefore not be the
- * output of the immediately preceding call into this library on the same stream
- * (put any other stream operation, e.g. an event record, in between).
+ * scales; for M <= 128 also the per-column w_scale and bias); every activation,
+ * activation scale, residual and output (and, for M > 128, w_scale and bias) is
+ * touched only after the preceding kernel has completed.  A weight, w_scale or
+ * bias must therefore not be the output of the immediately preceding call into
+ * this library on the same stream (put any other stream operation, e.g. an event
+ * record, in between).
  */
 #ifndef ISP_B200_H
 #define ISP_B200_H

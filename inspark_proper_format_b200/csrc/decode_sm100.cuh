@@ -25,7 +25,8 @@ namespace isp {
 namespace gemm {
 
 constexpr int kDecBN = 128;
-constexpr int kDecStages = 4;
+constexpr int kDecStages = 6;            // up to 6 K blocks per CTA: every weight tile is requested before the wait
+constexpr int kDecMaxSplits = 8;
 constexpr int kDecThreads = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 TMEM -> shared
 constexpr int kDecRowStride = 528;        // bytes per partial row: 128 x 4 B + 16 B (conflict-free 16-byte stores)
 
@@ -33,10 +34,17 @@ struct DecSmem {
   static constexpr int kABytes = kBM * kBK;        // 16 KB
   static constexpr int kBBytes = kDecBN * kBK;     // 16 KB
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kRedOffset = kDecStages * kStageBytes;
+  // The partial sums reuse the stage buffers: they are written after the CTA's
+  // last MMA has completed, and with it every TMA load those MMAs consumed.
+  static constexpr int kRedOffset = 0;
   static constexpr int kRedBytes = kBM * kDecRowStride;
-  static constexpr int kBarOffset = kRedOffset + kRedBytes;
+  // Epilogue operands staged in shared memory: w_scale and bias of the tile's
+  // columns (read before the programmatic-dependency wait), the scale of each row.
+  static constexpr int kParamOffset = kDecStages * kStageBytes;
+  static constexpr int kParamBytes = (2 * kDecBN + kBM) * 4;
+  static constexpr int kBarOffset = kParamOffset + kParamBytes;
   static constexpr int kBytes = kBarOffset + 128;
+  static_assert(kRedBytes <= kDecStages * kStageBytes, "partials must fit in the stage buffers");
 };
 
 // cluster_rank, cluster_sync_all and map_to_rank are in gemm_sm100.cuh
@@ -57,9 +65,7 @@ ISP_D float dec_acc(uint32_t bits) {
 
 // The regular kernel's EPI_SCALE arithmetic for one value (see scale_group).
 template <bool kInt8>
-ISP_D float dec_scale(float acc, const Params& p, float sa, int n) {
-  const float ws = p.w_scale != nullptr ? __ldg(p.w_scale + n) : 1.f;
-  const float b = p.bias != nullptr ? __ldg(p.bias + n) : 0.f;
+ISP_D float dec_scale(float acc, const Params& p, float sa, float ws, float b) {
   if (p.a_scale_rows != nullptr) {
     if constexpr (kInt8) return __fadd_rn(__fmul_rn(acc, __fmul_rn(sa, ws)), b);
     else return __fmaf_rn(__fmul_rn(acc, sa), ws, b);
@@ -83,6 +89,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint8_t* red = smem + L::kRedOffset;
+  float* ws_s = reinterpret_cast<float*>(smem + L::kParamOffset);
+  float* bias_s = ws_s + kDecBN;
+  float* sa_s = bias_s + kDecBN;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -124,15 +133,30 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       tma_load_2d(sa + L::kABytes, &tm_b, &full_bar[i], (kb0 + i) * kBK, n0);
     }
   }
+  if (warp >= 2) {   // per-column weight scale and bias: weights, like the tiles above
+    const int c = threadIdx.x - 64;
+    const int n = n0 + c;
+    ws_s[c] = (p.w_scale != nullptr && n < p.N) ? __ldg(p.w_scale + n) : 1.f;
+    bias_s[c] = (p.bias != nullptr && n < p.N) ? __ldg(p.bias + n) : 0.f;
+  }
   pdl_wait();      // predecessor complete before any activation or output access
   pdl_trigger();
+  if (warp >= 2) {
+    const int m = threadIdx.x - 64;
+    sa_s[m] = p.a_scale_rows != nullptr ? (m < p.M ? __ldg(p.a_scale_rows + m) : 0.f) : p.a_scale;
+  }
 
   if (warp == 0 && run) {
     // ------------------------------------------------------------ producer
     int stage = 0;
     uint32_t phase = 0;
-    bool armed[kDecStages] = {false, false, false, false};
-    uint32_t armed_phase[kDecStages] = {0, 0, 0, 0};
+    bool armed[kDecStages];
+    uint32_t armed_phase[kDecStages];
+#pragma unroll
+    for (int s = 0; s < kDecStages; ++s) {
+      armed[s] = false;
+      armed_phase[s] = 0;
+    }
     for (int kb = kb0; kb < kb1; ++kb) {
       const bool pre = kb - kb0 < npre;       // stage armed and its weight tile issued above
       if (!pre && !wait_warp(&empty_bar[stage], phase ^ 1u, abort_flag)) break;
@@ -211,31 +235,40 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       const int n = n0 + c;
       if (n >= p.N) continue;                  // N % 16 == 0: a 4-column group is wholly in or out
       const uint32_t local = smem_u32(red + m * kDecRowStride + c * 4);
+      // all of the cluster's partials of this group requested before the first is used
+      uint4 t[kDecMaxSplits];
+#pragma unroll
+      for (int q = 0; q < kDecMaxSplits; ++q)
+        if (q < splits) t[q] = ld_cluster_v4(map_to_rank(local, q));
       float v[4];
       if constexpr (kInt8) {
         int32_t s4[4] = {0, 0, 0, 0};
-        for (int q = 0; q < splits; ++q) {
-          const uint4 t = ld_cluster_v4(map_to_rank(local, q));
-          s4[0] += static_cast<int32_t>(t.x); s4[1] += static_cast<int32_t>(t.y);
-          s4[2] += static_cast<int32_t>(t.z); s4[3] += static_cast<int32_t>(t.w);
+#pragma unroll
+        for (int q = 0; q < kDecMaxSplits; ++q) {
+          if (q < splits) {
+            s4[0] += static_cast<int32_t>(t[q].x); s4[1] += static_cast<int32_t>(t[q].y);
+            s4[2] += static_cast<int32_t>(t[q].z); s4[3] += static_cast<int32_t>(t[q].w);
+          }
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[j] = static_cast<float>(s4[j]);
       } else {
         float s4[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int q = 0; q < splits; ++q) {
-          const uint4 t = ld_cluster_v4(map_to_rank(local, q));
-          s4[0] = __fadd_rn(s4[0], __uint_as_float(t.x)); s4[1] = __fadd_rn(s4[1], __uint_as_float(t.y));
-          s4[2] = __fadd_rn(s4[2], __uint_as_float(t.z)); s4[3] = __fadd_rn(s4[3], __uint_as_float(t.w));
+#pragma unroll
+        for (int q = 0; q < kDecMaxSplits; ++q) {
+          if (q < splits) {
+            s4[0] = __fadd_rn(s4[0], __uint_as_float(t[q].x)); s4[1] = __fadd_rn(s4[1], __uint_as_float(t[q].y));
+            s4[2] = __fadd_rn(s4[2], __uint_as_float(t[q].z)); s4[3] = __fadd_rn(s4[3], __uint_as_float(t[q].w));
+          }
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[j] = s4[j];
       }
-      const float sa = p.a_scale_rows != nullptr ? __ldg(p.a_scale_rows + m) : p.a_scale;
+      const float sa = sa_s[m];
       const int64_t off = static_cast<int64_t>(m) * p.N + n;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        v[j] = dec_scale<kInt8>(v[j], p, sa, n + j);
+        v[j] = dec_scale<kInt8>(v[j], p, sa, ws_s[c + j], bias_s[c + j]);
         if (p.residual != nullptr) {
           const float r = p.residual_f32 ? __ldg(static_cast<const float*>(p.residual) + off + j)
                                          : __bfloat162float(static_cast<const __nv_bfloat16*>(p.residual)[off + j]);

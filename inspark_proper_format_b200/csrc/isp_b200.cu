@@ -761,7 +761,7 @@ int isp_scaled_gemm(const void* A, const void* W, int ab_dtype, int64_t M, int N
     p.residual_f32 = residual_dtype == ISP_F32;
     p.out = out;
     const int n_tiles = (N + kDecBN - 1) / kDecBN;
-    int splits = 8;
+    int splits = kDecMaxSplits;
     while (splits > 1 && (n_tiles * splits > isp::sm_count() || splits > p.k_blocks)) splits >>= 1;
     return ab_dtype == ISP_I8 ? dispatch_decode<true>(out_kind, ta, tb, p, splits, n_tiles, stream)
                               : dispatch_decode<false>(out_kind, ta, tb, p, splits, n_tiles, stream);

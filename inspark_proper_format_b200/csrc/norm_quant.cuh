@@ -175,24 +175,21 @@ ISP_D void norm_quant_row(const NormQuantParams& p, int64_t row, int lane, float
             v[i][j] = y.x;
             v[i][j + 1] = y.y;
           }
-          continue;
-        }
+        } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float y = v[i][j];
-          if constexpr (kNorm == ISP_NORM_RMS_GPTFAST) {
-            if constexpr (!kBF16) y = __fmul_rn(y, r);   // (BF16: normalized and rounded above)
-            y = __fmul_rn(y, gm[j]);
-            if (p.ada_w != nullptr) y = __fadd_rn(__fmul_rn(aw[j], y), ab[j]);
-          } else if constexpr (kNorm == ISP_NORM_RMS_QWEN) {
-            y = __fmul_rn(y, r);
-            y = __fmul_rn(y, gm[j]);
-            if constexpr (kBF16) y = bf16_round(y);
-          } else {
-            y = __fmul_rn(y, r);
-            if constexpr (kBF16) y = bf16_round(y);
+          for (int j = 0; j < 8; ++j) {
+            float y = __fmul_rn(v[i][j], r);
+            if constexpr (kNorm == ISP_NORM_RMS_GPTFAST) {    // FP32 input: no intermediate rounding
+              y = __fmul_rn(y, gm[j]);
+              if (p.ada_w != nullptr) y = __fadd_rn(__fmul_rn(aw[j], y), ab[j]);
+            } else if constexpr (kNorm == ISP_NORM_RMS_QWEN) {
+              y = __fmul_rn(y, gm[j]);
+              if constexpr (kBF16) y = bf16_round(y);
+            } else {
+              if constexpr (kBF16) y = bf16_round(y);
+            }
+            v[i][j] = y;
           }
-          v[i][j] = y;
         }
       }
     }
