@@ -1362,20 +1362,30 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         sched.coords(p, sched.begin, mt, nt, hn);
         tp.fetch(p, nt * kOutCols + (hn > 0 ? kOutCols / 2 : 0), et);
       }
+      int staged_n0 = -1;                        // first column of the parameters in shared memory
       for (int t = sched.begin; t < sched.end; t += sched.step) {
         int mt, nt, hn;
         sched.coords(p, t, mt, nt, hn);
         const int m0 = mt * kTileM + static_cast<int>(rank) * kBM;     // this CTA's 128 rows of the tile
         const int n0 = nt * kOutCols + (hn > 0 ? kOutCols / 2 : 0);   // half-N tile: its columns
-        // Per-column parameters of this tile -> shared memory (zero past column N),
-        // then start fetching the next tile's.
-        epilogue_sync<R::kEpiThreads>();
-        tp.store(params, et);
-        epilogue_sync<R::kEpiThreads>();
-        if (t + sched.step < sched.end) {
-          int mt2, nt2, hn2;
-          sched.coords(p, t + sched.step, mt2, nt2, hn2);
-          tp.fetch(p, nt2 * kOutCols + (hn2 > 0 ? kOutCols / 2 : 0), et);
+        // Per-column parameters -> shared memory (zero past column N) only when this
+        // tile's columns differ from the staged ones (a B-stationary range keeps one N
+        // tile for many consecutive tiles, so the two epilogue barriers are rare); then
+        // start fetching those of the next tile with different columns.
+        if (n0 != staged_n0) {
+          epilogue_sync<R::kEpiThreads>();
+          tp.store(params, et);
+          epilogue_sync<R::kEpiThreads>();
+          staged_n0 = n0;
+          for (int t2 = t + sched.step; t2 < sched.end; t2 += sched.step) {
+            int mt2, nt2, hn2;
+            sched.coords(p, t2, mt2, nt2, hn2);
+            const int c2 = nt2 * kOutCols + (hn2 > 0 ? kOutCols / 2 : 0);
+            if (c2 != n0) {
+              tp.fetch(p, c2, et);
+              break;
+            }
+          }
         }
         if (!wait_bounded(&tfull_bar[acc], acc_phase, abort_flag)) break;
         tc_fence_after();
