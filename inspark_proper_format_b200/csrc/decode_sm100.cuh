@@ -181,14 +181,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     for (int kb = kb0; kb < kb1; ++kb) {
       if (!wait_warp(&full_bar[stage], phase, abort_flag)) break;
       tc_fence_after();
-      if (lane == 0) {
+      {   // the whole warp: operands computed warp-wide, one elected lane issues
         const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
         const uint32_t b_addr = a_addr + L::kABytes;
 #pragma unroll
         for (int kk = 0; kk < kBK / 32; ++kk)
-          mma_issue<kInt8>(tmem_base, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
-                           (kb > kb0 || kk > 0) ? 1u : 0u);
-        mma_commit(&empty_bar[stage]);
+          mma_issue_elect<kInt8, false>(tmem_base, smem_desc_sw128(a_addr + kk * 32),
+                                        smem_desc_sw128(b_addr + kk * 32), idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+        mma_commit_elect<false>(&empty_bar[stage]);
       }
       __syncwarp();
       if (++stage == kDecStages) { stage = 0; phase ^= 1u; }
