@@ -789,7 +789,7 @@ def main():
     host_out = [torch.empty(stack.output.shape, dtype=stack.output.dtype).pin_memory() for _ in sets]
     compute = torch.cuda.current_stream(device)
     up_stream, down_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    n_e2e = max(3, args.steps // 2)
+    n_e2e = max(3, args.steps)                               # as many steps as the device-timed region
     stack_calls_per_step = list(stack.calls)
 
     def e2e_pass(n):
@@ -828,7 +828,9 @@ def main():
     e2e_pass(2)                                              # warm the copy streams
     torch.cuda.synchronize(device)
     barrier()
-    e2e_total = ctx.max_over_ranks(e2e_pass(n_e2e), device=device)
+    with ClockSampler(gpu_index) as e2e_clocks:
+        e2e_seconds = e2e_pass(n_e2e)
+    e2e_total = ctx.max_over_ranks(e2e_seconds, device=device)
     e2e_value = strong_scaling_throughput(job_flops * n_e2e, e2e_total) / 1e12
     out_ok = bool(torch.equal(host_out[(n_e2e - 1) % 2].to(device), sets[(n_e2e - 1) % 2]["out"]))
     h2d = host_in.numel() * host_in.element_size()
@@ -863,7 +865,8 @@ def main():
                 "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * d2h,
                 "per_gpu_bytes_each_way": h2d, "steps": n_e2e, "result_read_back_ok": out_ok,
                 "mode": "double-buffered: uploads/downloads on copy streams overlap neighbouring steps' compute; "
-                        "L2 flushed (256 MiB write) before every step inside the timed region"},
+                        "L2 flushed (256 MiB write) before every step inside the timed region",
+                "clocks": e2e_clocks.summary()},
         "clocks": clocks.summary(),
         "components": components,
     }

@@ -51,6 +51,11 @@ struct Roles {
   static constexpr int kThreads = 64 + kEpiThreads;
   static constexpr int kHalves = kEpiWarps / 4;
 };
+// NVFP4 kernels add one warp after the epilogue warps that copies each stage's block
+// scales into TMEM (tcgen05.cp costs the issuing thread ~115 cycles, more than the
+// K = 64 MMA it feeds), so the MMA warp issues only MMAs.
+template <int kEpiWarps, bool kFp4>
+constexpr int kernel_threads() { return Roles<kEpiWarps>::kThreads + (kFp4 ? 32 : 0); }
 
 enum AbKind { AB_E4M3 = 0, AB_I8 = 1, AB_FP4 = 2 };
 // EPI_CONV: the scale epilogue of a phase-folded implicit-GEMM convolution (A rows =
@@ -148,7 +153,7 @@ struct Smem {
   static constexpr int kParamOffset = kStagingOffset + kStagingBytes;
   static constexpr int kParamBytes = 512 * 4;              // per-tile column scales / bias
   static constexpr int kBarOffset = kParamOffset + kParamBytes;
-  static constexpr int kBytes = kBarOffset + 256;          // + barriers/flags (base is 1024-aligned)
+  static constexpr int kBytes = kBarOffset + (kFp4 ? 384 : 256);   // + barriers/flags (base is 1024-aligned)
   static_assert(kStageBytes % 1024 == 0 && kBResOffset % 1024 == 0 && kStagingOffset % 1024 == 0,
                 "swizzled regions start 1024-byte aligned");
 };
@@ -914,7 +919,7 @@ struct Schedule {
 // bytes of both CTAs and both CTAs' epilogue hand-backs are counted there); the leader's
 // commits arrive on the empty / bempty / tfull / drain barriers of both CTAs.
 template <int kBN, int kStages, int kEpiWarps, int kAB, int kEpi, int kOut, int kBStatK, bool kPair>
-__global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
+__global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_out,
                 const __grid_constant__ Params p) {
@@ -950,7 +955,8 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
   uint64_t* drain_bar = tempty_bar + 2;          // [1]
   uint64_t* bfull_bar = drain_bar + 1;           // [1] resident B landed (B-stationary)
   uint64_t* bempty_bar = bfull_bar + 1;          // [1] every MMA reading the resident B completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bempty_bar + 1);
+  uint64_t* sf_bar = bempty_bar + 1;            // [kStages] NVFP4: the stage's scales are in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_bar + (kFp4 ? kStages : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -975,6 +981,8 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
     mbar_init(drain_bar, 1);
     mbar_init(bfull_bar, 1);
     mbar_init(bempty_bar, 1);
+    if constexpr (kFp4)
+      for (int s = 0; s < kStages; ++s) mbar_init(&sf_bar[s], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tm_a);
@@ -1136,6 +1144,43 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         if (kStat && nloads > 0) wait_warp_drain(bfull_bar, (nloads - 1) & 1u);
       }
     }
+  } else if (kFp4 && warp == kEpiWarp0 + kEpiWarps) {
+    // ------------------------------------------------------------ scale copies (NVFP4)
+    // Walks the MMA warp's stage sequence: once a stage has landed, its block scales
+    // (A; streaming also B) go to the stage's TMEM scale columns and a commit on
+    // sf_bar[stage] signals their completion.  A stage's columns are rewritten only
+    // after its next TMA load, i.e. after the MMAs of its previous use completed.
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    bool armed[kStages];
+    uint32_t armed_phase[kStages];
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) armed[s] = false, armed_phase[s] = 0;
+    for (int t = sched.begin; t < sched.end && ok; t += sched.step) {
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        if (!wait_warp(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        {
+          const int nch = min(4, p.k_chunks - 4 * kb);
+          const uint32_t sfa_t = tmem_base + static_cast<uint32_t>(2 * kBN + kSfbResCols + (kStat ? 16 : 32) * stage);
+          const uint32_t sf_s = smem_u32(smem + L::sfa(stage));
+          for (int c = 0; c < nch; ++c) {
+            tmem_cp_sf_elect(sfa_t + 4 * c, smem_desc_sf(sf_s + c * kSfChunk));
+            if constexpr (!kStat)
+              tmem_cp_sf_elect(sfa_t + 16 + 4 * c, smem_desc_sf(smem_u32(smem + L::sfb(stage)) + c * kSfChunk));
+          }
+          mma_commit_elect<false>(&sf_bar[stage]);
+        }
+        __syncwarp();
+        armed[stage] = true;
+        armed_phase[stage] = phase;
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+    // Drain: every issued copy has completed before TMEM is released (also on abort).
+    for (int s = 0; s < kStages; ++s)
+      if (armed[s]) wait_warp_drain(&sf_bar[s], armed_phase[s]);
   } else if (warp == 1 && kPair && !leader) {
     // pair peer: no MMAs here; before the CTA may retire, wait for the leader's final
     // commit (every MMA reading this CTA's shared memory has completed)
@@ -1184,23 +1229,19 @@ __global__ void __launch_bounds__(Roles<kEpiWarps>::kThreads, 1)
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!wait_warp(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          if constexpr (kFp4)   // the scale warp's copies of this stage have completed
+            if (!wait_warp(&sf_bar[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
           {   // the whole warp: operands computed warp-wide, one elected lane issues
             const uint32_t a_addr = smem_u32(smem + L::a(stage));
             const uint32_t b_addr =
                 kStat ? smem_u32(smem + L::kBResOffset + kb * L::kBBytes) : smem_u32(smem + L::b(stage));
             if constexpr (kFp4) {
-              // Scales -> TMEM, then one K = 64 MMA per chunk; tcgen05.cp and
-              // tcgen05.mma issued by one thread execute in order.
+              // One K = 64 MMA per scale chunk; the chunks are in this stage's TMEM
+              // scale columns (copied by the scale warp, completion on sf_bar).
               const int nch = min(4, p.k_chunks - 4 * kb);
               const uint32_t sfa_t =
                   tmem_base + static_cast<uint32_t>(2 * kBN + kSfbResCols + (kStat ? 16 : 32) * stage);
-              const uint32_t sf_s = smem_u32(smem + L::sfa(stage));
-              for (int c = 0; c < nch; ++c) {
-                tmem_cp_sf_elect(sfa_t + 4 * c, smem_desc_sf(sf_s + c * kSfChunk));
-                if constexpr (!kStat)
-                  tmem_cp_sf_elect(sfa_t + 16 + 4 * c, smem_desc_sf(smem_u32(smem + L::sfb(stage)) + c * kSfChunk));
-              }
               for (int kk = 0; kk < nch; ++kk) {
                 const uint32_t sfb_t = kStat ? sfb_res_t + 4 * (4 * kb + kk) : sfa_t + 16 + 4 * kk;
                 mma_fp4_elect(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,

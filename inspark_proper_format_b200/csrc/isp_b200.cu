@@ -202,7 +202,7 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, co
       // persistent pairs: no more clusters than can be resident at once
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (sm_count() / 2));
-      cfg.blockDim = dim3(Roles<kEpiWarps>::kThreads);
+      cfg.blockDim = dim3(kernel_threads<kEpiWarps, kAB == AB_FP4>());
       cfg.dynamicSmemBytes = kSmem;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -224,11 +224,11 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, co
   if constexpr (kPair) {
     const int cap = (dev >= 0 && dev < 64 && max_pairs[dev] > 0) ? max_pairs[dev] : sm_count() / 2;
     const int pairs = tiles < cap ? tiles : cap;
-    return launch_pdl_cluster(kern, dim3(2 * pairs), dim3(Roles<kEpiWarps>::kThreads), kSmem, stream, 2u, a, b, b2,
+    return launch_pdl_cluster(kern, dim3(2 * pairs), dim3(kernel_threads<kEpiWarps, kAB == AB_FP4>()), kSmem, stream, 2u, a, b, b2,
                               o, p);
   }
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  return launch_pdl(kern, dim3(grid), dim3(Roles<kEpiWarps>::kThreads), kSmem, stream, a, b, b2, o, p);
+  return launch_pdl(kern, dim3(grid), dim3(kernel_threads<kEpiWarps, kAB == AB_FP4>()), kSmem, stream, a, b, b2, o, p);
 }
 
 // Schedules: 0 streaming, 1 B-stationary (one CTA per tile), 2 B-stationary SM pairs.
