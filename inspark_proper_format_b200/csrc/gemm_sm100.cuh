@@ -950,9 +950,12 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
   float* params = reinterpret_cast<float*>(smem + L::kParamOffset);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* empty_bar = full_bar + kStages;
-  uint64_t* tfull_bar = empty_bar + kStages;     // [2]
-  uint64_t* tempty_bar = tfull_bar + 2;          // [2]
-  uint64_t* drain_bar = tempty_bar + 2;          // [1]
+  // TMEM accumulators: two; B-stationary NVFP4 tiles (one 128-column accumulator per
+  // 512 MMA cycles, shorter than the accumulator hand-back round trip) keep three.
+  constexpr int kAccs = (kFp4 && kStat) ? 3 : 2;
+  uint64_t* tfull_bar = empty_bar + kStages;     // [kAccs]
+  uint64_t* tempty_bar = tfull_bar + kAccs;      // [kAccs]
+  uint64_t* drain_bar = tempty_bar + kAccs;      // [1]
   uint64_t* bfull_bar = drain_bar + 1;           // [1] resident B landed (B-stationary)
   uint64_t* bempty_bar = bfull_bar + 1;          // [1] every MMA reading the resident B completed
   uint64_t* sf_bar = bempty_bar + 1;            // [kStages] NVFP4: the stage's scales are in TMEM
@@ -966,15 +969,21 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
   // (4 per 64-element K chunk) and 16 A columns per stage.
   // (allocations are powers of two: two 192-column nonlinear-value accumulators take 512)
   constexpr int kTmemCols = (kFp4 || kEpi == EPI_NLV) ? 512 : 2 * kBN;
+  // NVFP4 scale columns of a stage's A (streaming: A and B) scales; with three
+  // accumulators the stages share four slots, a slot being rewritten only after the
+  // MMAs of its previous stage completed (the scale warp waits for that stage's empty
+  // barrier).
+  constexpr int kSfSlots = kAccs == 3 ? 4 : kStages;
+  static_assert(kSfSlots <= kStages, "a slot's previous stage is at most one ring round back");
   constexpr int kSfbResCols = kStat ? (2 * kBStatK / 64) * 4 : 0;
-  static_assert(!kFp4 || 2 * kBN + kSfbResCols + (kStat ? 16 : 32) * kStages <= 512, "TMEM columns");
+  static_assert(!kFp4 || kAccs * kBN + kSfbResCols + (kStat ? 16 : 32) * kSfSlots <= 512, "TMEM columns");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kAccs; ++a) {
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], kPair ? 2 * kEpiWarps : kEpiWarps);   // one arrive per epilogue warp
     }
@@ -1157,13 +1166,23 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
     uint32_t armed_phase[kStages];
 #pragma unroll
     for (int s = 0; s < kStages; ++s) armed[s] = false, armed_phase[s] = 0;
+    int uses = 0;                                   // stages consumed so far
+    int slot = 0;                                   // = uses mod kSfSlots
     for (int t = sched.begin; t < sched.end && ok; t += sched.step) {
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         if (!wait_warp(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+        if (kSfSlots < kStages && uses >= kSfSlots) {
+          // the MMAs of the stage that last used this slot have completed
+          const int prev = stage >= kSfSlots ? stage - kSfSlots : stage + kStages - kSfSlots;
+          const uint32_t prev_phase = stage >= kSfSlots ? phase : phase ^ 1u;
+          if (!wait_warp(&empty_bar[prev], prev_phase, abort_flag)) { ok = false; break; }
+        }
+        ++uses;
         tc_fence_after();
         {
           const int nch = min(4, p.k_chunks - 4 * kb);
-          const uint32_t sfa_t = tmem_base + static_cast<uint32_t>(2 * kBN + kSfbResCols + (kStat ? 16 : 32) * stage);
+          const uint32_t sfa_t =
+              tmem_base + static_cast<uint32_t>(kAccs * kBN + kSfbResCols + (kStat ? 16 : 32) * slot);
           const uint32_t sf_s = smem_u32(smem + L::sfa(stage));
           for (int c = 0; c < nch; ++c) {
             tmem_cp_sf_elect(sfa_t + 4 * c, smem_desc_sf(sf_s + c * kSfChunk));
@@ -1175,6 +1194,7 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
         __syncwarp();
         armed[stage] = true;
         armed_phase[stage] = phase;
+        if (++slot == kSfSlots) slot = 0;
         if (++stage == kStages) { stage = 0; phase ^= 1u; }
       }
     }
@@ -1187,12 +1207,13 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
     wait_warp_drain(drain_bar, 0);
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // The whole warp runs the loop (waits converged); lane 0 issues tcgen05 ops.
+    // The whole warp runs the loop (waits converged); one elected lane issues tcgen05 ops.
     {
       const uint32_t idesc = instr_desc<kAB, kBN, kTileM>();
       const uint32_t idesc_half = instr_desc<kAB, kBN / 2>();   // half-N tiles of the split tail
-      const uint32_t sfb_res_t = tmem_base + static_cast<uint32_t>(2 * kBN);   // B-stationary NVFP4
+      const uint32_t sfb_res_t = tmem_base + static_cast<uint32_t>(kAccs * kBN);   // B-stationary NVFP4
       int stage = 0;
+      int sf_slot = 0;                           // NVFP4 scale slot: stages consumed mod kSfSlots
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
@@ -1241,7 +1262,7 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
               // scale columns (copied by the scale warp, completion on sf_bar).
               const int nch = min(4, p.k_chunks - 4 * kb);
               const uint32_t sfa_t =
-                  tmem_base + static_cast<uint32_t>(2 * kBN + kSfbResCols + (kStat ? 16 : 32) * stage);
+                  tmem_base + static_cast<uint32_t>(kAccs * kBN + kSfbResCols + (kStat ? 16 : 32) * sf_slot);
               for (int kk = 0; kk < nch; ++kk) {
                 const uint32_t sfb_t = kStat ? sfb_res_t + 4 * (4 * kb + kk) : sfa_t + 16 + 4 * kk;
                 mma_fp4_elect(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
@@ -1261,12 +1282,13 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
           }
           __syncwarp();
           issued = true;
+          if (++sf_slot == kSfSlots) sf_slot = 0;
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
         mma_commit_elect<kPair>(&tfull_bar[acc]);
         __syncwarp();
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
       }
       // Drain: all issued MMAs have completed before TMEM is released (also on abort).
       if (issued) {
@@ -1325,7 +1347,7 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
         const int m = mt * kBM + row_in_tile;
         if (m >= p.M) continue;
         const int c0 = half * 32;
@@ -1390,7 +1412,7 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
           p.q_sf[(static_cast<int64_t>(m >> 7) * (p.N / 64) + (n >> 6)) * kSfChunk + (m & 31) * 16 +
                  ((m >> 5) & 3) * 4 + ((n >> 4) & 3)] = static_cast<uint8_t>(sc);
         }
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
       }
     } else {
       const int half = ew / 4;                     // which share of the columns (8-warp epilogue)
@@ -1449,7 +1471,7 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
             if constexpr (kPair) mbar_arrive_cluster(map_to_rank(smem_u32(&tempty_bar[acc]), 0));
             else mbar_arrive(&tempty_bar[acc]);
           }
-          if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+          if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
           continue;
         }
         const int m = m0 + row_in_tile;
@@ -1579,7 +1601,7 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
             }
           }
         }
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
       }
       if (lane == 0) bulk_wait_all();
       __syncwarp();
