@@ -381,14 +381,26 @@ ISP_D void mbar_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes) {
 }
 // SM-pair tile load: the box lands in this CTA's shared memory and its bytes are
 // counted on the barrier at `bar_cluster_addr` (the pair leader's), where the MMA
-// that reads both CTAs' halves waits.  No multicast.  Loaded with the evict-last
-// L2 policy (measured: 2 us less per M = 48640, N = 1536 launch than no hint).
+// that reads both CTAs' halves waits.  No multicast.  kEvictLast: loaded with the
+// evict-last L2 policy, for tiles re-read by later tiles of the launch (B-stationary
+// A: 2 us less per M = 48640, N = 1536 launch than no hint; streamed weights); the
+// streamed A of a K > 512 GEMM (75 MB at M = 48640, K = 1536) is loaded without a hint,
+// since evict-last there pushes the next kernel's data out of L2.
+template <bool kEvictLast>
 ISP_D void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster_addr, int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
-      "[%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "l"(policy_evict_last())
-      : "memory");
+  if constexpr (kEvictLast) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+        "[%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "l"(policy_evict_last())
+        : "memory");
+  } else {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], "
+        "[%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
+        : "memory");
+  }
 }
 // Commit of the leader's SM-pair MMAs: one arrive on the barrier at this offset in
 // both CTAs of the pair once every MMA issued before it has completed.
@@ -931,8 +943,8 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
   static_assert(kBStatK % kBK == 0, "resident K is whole 128-byte blocks");
   static_assert(kEpi != EPI_NLV || (kBN == kNlvBN && kAB == AB_I8 && kOut == OUT_F32 && kEpiWarps == 8),
                 "nonlinear-value tiles: INT8, 3 x 64 columns, FP32 outputs, two epilogue warps per lane quarter");
-  static_assert(!kPair || (kStat && kEpi == EPI_SCALE && !kFp4 && kBN == 256),
-                "SM-pair tiles: B-stationary 256 x 256 FP8 / INT8 scale GEMMs");
+  static_assert(!kPair || (kEpi == EPI_SCALE && !kFp4 && kBN == 256),
+                "SM-pair tiles: 256 x 256 FP8 / INT8 scale GEMMs (B-stationary or streaming)");
   constexpr int kBRows = kPair ? kBN / 2 : kBN;   // B rows in this CTA's shared memory
   constexpr int kTileM = kPair ? 2 * kBM : kBM;   // rows of one tile
   constexpr int kStagingBufs = kPair ? kStagingBufsPair : kStagingBufsOne;
@@ -1032,7 +1044,7 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
     for (int kb = 0; kb < p.k_blocks && lane == 0; ++kb) {
       uint8_t* dst = smem + L::kBResOffset + kb * L::kBBytes;
       if constexpr (kPair) {
-        tma_load_2d_pair(dst, &tm_b, map_to_rank(smem_u32(bfull_bar), 0), kb * kBK,
+        tma_load_2d_pair<true>(dst, &tm_b, map_to_rank(smem_u32(bfull_bar), 0), kb * kBK,
                          nt * kBN + static_cast<int>(rank) * kBRows);
       } else if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
         tma_load_2d(dst, &tm_b, bfull_bar, kb * kBK, nt * (kBN / 2));
@@ -1104,7 +1116,7 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
             if constexpr (kFp4) bytes += static_cast<uint32_t>(nch) * kSfChunk * (kStat ? 1 : 2);
             if constexpr (kPair) {
               if (leader) mbar_expect_tx(&full_bar[stage], 2 * bytes);
-              tma_load_2d_pair(sa, &tm_a, map_to_rank(smem_u32(&full_bar[stage]), 0), kb * kBK, m0);
+              tma_load_2d_pair<kStat>(sa, &tm_a, map_to_rank(smem_u32(&full_bar[stage]), 0), kb * kBK, m0);
             } else {
               mbar_expect_tx(&full_bar[stage], bytes);
             }
@@ -1124,7 +1136,10 @@ __global__ void __launch_bounds__(kernel_threads<kEpiWarps, kAB == AB_FP4>(), 1)
             }
             if constexpr (!kStat) {
               uint8_t* sb = smem + L::b(stage);
-              if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
+              if constexpr (kPair) {   // this CTA's half of the stage's B rows, bytes on the leader's barrier
+                tma_load_2d_pair<true>(sb, &tm_b, map_to_rank(smem_u32(&full_bar[stage]), 0), kb * kBK,
+                                 nt * kBN + static_cast<int>(rank) * kBRows);
+              } else if constexpr (kEpi == EPI_SWIGLU_PAIRED && !kFp4) {
                 tma_load_2d(sb, &tm_b, &full_bar[stage], kb * kBK, nt * (kBN / 2));
                 tma_load_2d(sb + (kBN / 2) * kBK, &tm_b2, &full_bar[stage], kb * kBK, nt * (kBN / 2));
               } else if constexpr (kEpi == EPI_NLV) {

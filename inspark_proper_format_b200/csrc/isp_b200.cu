@@ -154,6 +154,9 @@ constexpr int kNlvStatStages = 6;      // INT8 nonlinear value: 6 x 16 KB of A +
 #define ISP_GEMM_PAIR_STAGES 6
 #endif
 constexpr int kPairStages = ISP_GEMM_PAIR_STAGES;
+// Streaming SM pairs (K > 512 bytes): a stage is 16 KB of A and 16 KB of B (this CTA's
+// half of the 256 B rows); five stages beside two staging boxes per epilogue warp.
+constexpr int kPairStreamStages = 5;
 
 // Schedule overrides for A/B measurements, fixed at compile time (e.g.
 // -DISP_GEMM_FORCE_STREAMING=1); the shipped library defines none of them, so it
@@ -162,7 +165,7 @@ constexpr int kPairStages = ISP_GEMM_PAIR_STAGES;
 //   ISP_GEMM_NO_TAIL_SPLIT    keep the last partial wave of streaming GEMMs as whole tiles
 //   ISP_CONV_DIRECT_STORE     per-element stores in the convolution epilogue
 //   ISP_GEMM_NO_DECODE        the regular kernel for M <= 128 instead of cluster split-K
-//   ISP_GEMM_NO_PAIR          B-stationary scale GEMMs on one CTA per tile instead of SM pairs
+//   ISP_GEMM_NO_PAIR          scale GEMMs on one CTA per tile instead of SM pairs
 #ifndef ISP_GEMM_FORCE_STREAMING
 #define ISP_GEMM_FORCE_STREAMING 0
 #endif
@@ -232,7 +235,8 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2, co
 }
 
 // Schedules: 0 streaming, 1 B-stationary (one CTA per tile), 2 B-stationary SM pairs.
-enum Sched { SCHED_STREAM = 0, SCHED_STAT = 1, SCHED_PAIR = 2 };
+enum Sched { SCHED_STREAM = 0, SCHED_STAT = 1, SCHED_PAIR = 2, SCHED_PAIR_STREAM = 3 };
+constexpr bool sched_pair(int s) { return s == SCHED_PAIR || s == SCHED_PAIR_STREAM; }
 
 template <int kAB, int kOut>
 int launch_scale(int sched, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o, const Params& p,
@@ -244,6 +248,8 @@ int launch_scale(int sched, const CUtensorMap& a, const CUtensorMap& b, const CU
   } else {
     if (sched == SCHED_PAIR)
       return launch<kBN, kPairStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut, kStatK, true>(a, b, b, o, p, s);
+    if (sched == SCHED_PAIR_STREAM)
+      return launch<kBN, kPairStreamStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut, 0, true>(a, b, b, o, p, s);
     return sched == SCHED_STAT ? launch<kBN, kStatStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut, kStatK>(a, b, b, o, p, s)
                                : launch<kBN, kStages, kScaleEpiWarps, kAB, EPI_SCALE, kOut>(a, b, b, o, p, s);
   }
@@ -766,19 +772,21 @@ int isp_scaled_gemm(const void* A, const void* W, int ab_dtype, int64_t M, int N
     return ab_dtype == ISP_I8 ? dispatch_decode<true>(out_kind, ta, tb, p, splits, n_tiles, stream)
                               : dispatch_decode<false>(out_kind, ta, tb, p, splits, n_tiles, stream);
   }
-  // K <= 512 bytes: B-stationary; M > 128 rows on SM pairs (256-row tiles, half of B per SM)
+  // K <= 512 bytes: B-stationary, else B streamed through the ring; both on SM pairs
+  // (256-row tiles, half of B per SM)
   const bool stat = K <= kStatK && !streaming_forced();
-  const int sched = !stat ? SCHED_STREAM : (pair_schedule_enabled() ? SCHED_PAIR : SCHED_STAT);
+  const int sched = !stat ? (pair_schedule_enabled() ? SCHED_PAIR_STREAM : SCHED_STREAM)
+                          : (pair_schedule_enabled() ? SCHED_PAIR : SCHED_STAT);
   CUtensorMap ta, tb, to;
   if (!make_map(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, kBK, kBM) ||
-      !make_map(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, kBK, sched == SCHED_PAIR ? kBN / 2 : kBN) ||
+      !make_map(&tb, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, kBK, sched_pair(sched) ? kBN / 2 : kBN) ||
       !make_out_map(&to, out, out_kind, M, N))
     return ISP_ERR_ALIGN;
   Params p{};
   p.M = static_cast<int>(M);
   p.N = N;
   p.K = K;
-  p.m_tiles = static_cast<int>((M + (sched == SCHED_PAIR ? 2 * kBM : kBM) - 1) / (sched == SCHED_PAIR ? 2 * kBM : kBM));
+  p.m_tiles = static_cast<int>((M + (sched_pair(sched) ? 2 * kBM : kBM) - 1) / (sched_pair(sched) ? 2 * kBM : kBM));
   p.n_tiles = (N + kBN - 1) / kBN;
   p.k_blocks = (K + kBK - 1) / kBK;
   p.a_scale = a_scale;
@@ -792,7 +800,8 @@ int isp_scaled_gemm(const void* A, const void* W, int ab_dtype, int64_t M, int N
   p.out2_inv = out2_inv_scale;
   // streaming: the last partial wave runs as half-N tiles (needs the two-warps-per-quarter
   // epilogue, whose upper warps simply hand a half tile's accumulator back)
-  p.tail_split = !stat && kScaleEpiWarps == 8 && !tail_split_disabled();
+  // (single CTAs only: an SM pair's tile is not split)
+  p.tail_split = sched == SCHED_STREAM && kScaleEpiWarps == 8 && !tail_split_disabled();
   return ab_dtype == ISP_I8 ? dispatch_scale_out<AB_I8>(out_kind, sched, ta, tb, to, p, stream)
                             : dispatch_scale_out<AB_E4M3>(out_kind, sched, ta, tb, to, p, stream);
 }
